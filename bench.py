@@ -1,0 +1,377 @@
+"""Benchmark of the stencil hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl basalto|reference] [--workload NAME]
+    torchrun --nproc-per-node N bench.py --gpus N ...       (N > 1: one process per GPU)
+
+Workload (default): 2-D five-point Jacobi, fp32 8192 x 8192 ~U(-1,1) seed 1, Dirichlet-0
+ghost cells, 100 ping-pong sweeps.  One step = the full 100-sweep run.  At N > 1 every rank
+owns an 8192 x 8192 slab of a (8192*N) x 8192 grid split along rows (weak scaling): each
+sweep exchanges one ghost row with each neighbour over NCCL, overlapped with the interior.
+
+value      grid-point updates per second of the whole job (Gpts/s), inputs resident in HBM,
+           CUDA events on the compute stream, max over ranks.
+e2e        the same metric through the public plugin path: pinned host grid -> H2D ->
+           torch.compile(jacobi, backend="basalto") called once per sweep -> D2H, all inside
+           the timed region (N = 1; at N > 1 the slab API with host copies).
+roofline   the Jacobi kernel: algorithmic bytes (8 B per point: one read + one write) per
+           launch / average launch time, against the measured HBM copy bandwidth.
+cpu_baseline / --impl reference
+           the reference's CPU path: eager torch through the reference backend's control
+           flow (oracle/reference_path.py), all host threads, a bounded number of sweeps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "bs-compiler_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "stencil Gpts/s and % of HBM roofline at 1/2/4/8 B200 vs reference CPU path"
+UNIT = "Gpts/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _traffic(workload: str, kernel: str):
+    """Per-launch DRAM bytes of the kernel from a committed ncu summary, if one exists."""
+    p = REPO / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _init_pg(ws, rank, local, backend):
+    import datetime
+
+    import torch.distributed as dist
+    if ws > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+    return dist
+
+
+class CpuReference:
+    """Eager torch on the host through the reference backend's control flow."""
+
+    def __init__(self, workload, threads: int | None = None):
+        from oracle.reference_path import compile_reference
+        if threads:
+            torch.set_num_threads(threads)
+        self.w = workload
+        self.x = workload.make_input()  # CPU, the configuration's own seeded grid
+        self.cf = compile_reference(workload.fn)
+        self.y = self.cf(self.x)  # compile + one warm sweep
+
+    def rate(self, sweeps: int):
+        """(Gpts/s, seconds) over `sweeps` consecutive sweeps."""
+        y = self.y
+        t0 = time.perf_counter()
+        for _ in range(sweeps):
+            y = self.cf(y)
+        dt = time.perf_counter() - t0
+        self.y = y
+        return self.w.points * sweeps / dt / 1e9, dt
+
+
+def run_reference(args):
+    ws, rank, local = _dist()
+    from basalto.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    ref = CpuReference(w, threads)
+    per_step = max(1, args.ref_sweeps)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        r, dt = ref.rate(per_step)
+        if i >= args.warmup:
+            rates.append((r, dt))
+    value = statistics.median(r for r, _ in rates)
+    ms = statistics.median(dt for _, dt in rates) * 1e3 / per_step * w.steps
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if w.dtype == torch.float32 else "f64",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"{w.name} {'x'.join(map(str, w.shape))} {w.steps} sweeps",
+                   "sample": f"{per_step} sweep(s) per step on the full grid; ms_per_step scaled to {w.steps} sweeps"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{per_step} of {w.steps} sweeps per step, full {'x'.join(map(str, w.shape))} grid"},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_basalto(args):
+    import ctypes
+
+    import basalto
+    from basalto import _abi
+    from basalto.workloads import WORKLOADS
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = _init_pg(ws, rank, local, "nccl") if ws > 1 else None
+    w = WORKLOADS[args.workload]
+    prog = w.program
+    sweeps = w.steps
+    stream = torch.cuda.current_stream(dev)
+    es = w.elem_size
+
+    if ws == 1:
+        a = w.make_input(device=dev)
+        b = torch.empty_like(a)
+
+        def step():
+            basalto.sweeps(prog, a, b, sweeps)
+
+        points_job = w.points
+        launches_per_step = sweeps
+        comm = None
+    else:
+        # Weak scaling: each rank owns a full-size slab; ghost planes along axis 0.
+        R = prog.radius()[0]
+        local_shape = list(w.shape)
+        g = torch.Generator(device=dev).manual_seed(w.seed + 1000 * rank)
+        a = torch.zeros([local_shape[0] + 2 * R] + local_shape[1:], dtype=w.dtype, device=dev)
+        b = torch.zeros_like(a)
+        a[R:R + local_shape[0]].copy_(torch.rand(local_shape, generator=g, dtype=w.dtype, device=dev) * 2 - 1)
+        uid = (ctypes.c_uint8 * 128)()
+        obj = [None]
+        if rank == 0:
+            _abi.check(_abi.lib().bst_nccl_get_unique_id(uid))
+            obj[0] = bytes(uid)
+        dist.broadcast_object_list(obj, src=0)
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
+        h = ctypes.c_void_p()
+        _abi.check(_abi.lib().bst_comm_create(uid, ws, rank, local, 120.0, ctypes.byref(h)))
+        comm = h
+        cp = prog.to_c(local_shape)
+        dt = _abi.BST_F32 if w.dtype == torch.float32 else _abi.BST_F64
+        plane = 1
+        for s in local_shape[1:]:
+            plane *= s
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0], R, sp))
+        shp = _abi.i64_array(local_shape)
+
+        def step():
+            _abi.check(_abi.lib().bst_slab_sweeps(comm, ctypes.byref(cp), dt, len(local_shape), shp,
+                                                  ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                                                  sweeps, sp))
+
+        points_job = w.points * ws
+        launches_per_step = sweeps * (3 if local_shape[0] > 2 * R else 2)
+
+    # ---- timed region (device time, CUDA events on the compute stream) -------------------
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    n0 = basalto.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    launches = basalto.launch_count() - n0
+    clk = clocks.stop()
+    ms_total = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = points_job * sweeps * args.steps / (ms_total * 1e-3) / 1e9
+
+    # Dominant kernel: the sweep itself; average launch = timed region / sweeps (per rank).
+    launch_ms = ms_total / (args.steps * sweeps)
+    per_launch_bytes = 2 * es * w.points
+    achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
+    peak, peak_src = _peaks()
+
+    # ---- e2e through the plugin path with host buffers ------------------------------------
+    e2e = None
+    if ws == 1:
+        host_in = w.make_input().pin_memory() if args.host_input else torch.empty(w.shape, dtype=w.dtype).pin_memory()
+        host_out = torch.empty(w.shape, dtype=w.dtype).pin_memory()
+        torch._dynamo.reset()
+        cf = torch.compile(w.fn, backend="basalto")
+
+        def e2e_step():
+            x = host_in.to(dev, non_blocking=True)
+            for _ in range(sweeps):
+                x = cf(x)
+            host_out.copy_(x, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = f0.elapsed_time(f1) / args.e2e_steps
+        nbytes = w.points * es
+        e2e = {"value": round(w.points * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes, "ms_per_step": round(e_ms, 3),
+               "path": "torch.compile(backend='basalto'), one call per sweep, pinned host buffers"}
+
+    # ---- CPU baseline (rank 0, N = 1 only, bounded sample) ------------------------------------
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        r, dt = CpuReference(w, threads).rate(args.ref_sweeps)
+        cpu = {"value": round(r, 4), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{args.ref_sweeps} of {sweeps} sweeps on the full {'x'.join(map(str, w.shape))} grid, "
+                         f"eager torch via the reference backend's control flow ({dt:.1f} s)"}
+
+    if comm is not None:
+        torch.cuda.synchronize()
+        _abi.lib().bst_comm_destroy(comm)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32" if w.dtype == torch.float32 else "f64", "data": "synthetic",
+            "config": {"workload": f"{w.name} {'x'.join(map(str, w.shape))}{' per GPU' if ws > 1 else ''}, "
+                                   f"{sweeps} sweeps per step",
+                       "parallelism": f"z-slab x{ws}" if ws > 1 else "single GPU",
+                       "l2": f"inputs larger than L2 (2 x {w.points * es / 2**20:.0f} MiB ping-pong)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "traffic": _traffic(w.name, "march_tma_kernel"),
+                         "algorithmic_bytes_per_launch": per_launch_bytes, "avg_launch_ms": round(launch_ms, 5)},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "launches_expected": int(launches_per_step * args.steps),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="basalto", choices=["basalto", "reference"])
+    ap.add_argument("--workload", default="jacobi5_2d")
+    ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per CPU-baseline sample")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--host-input", action="store_true", default=True)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_basalto(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,316 @@
+// bst_halo.cu — Z-slab ghost-plane exchange over NCCL and the overlapped slab sweep.
+//
+// NCCL is bound at run time with dlopen (as crates/basalto-communication/src/nccl.rs:43-85
+// does), preferring the copy already loaded in the process (torch's), so a process never
+// mixes two NCCL builds.  Communicators are created non-blocking and polled with a host
+// timeout; on timeout they are aborted and an error is returned instead of hanging.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types and enums only; every call goes through the dlopen'd table
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "bst_internal.h"
+
+namespace bst {
+
+struct NcclApi {
+  void* lib = nullptr;
+  decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
+  decltype(&ncclCommInitRankConfig) CommInitRankConfig = nullptr;
+  decltype(&ncclCommGetAsyncError) CommGetAsyncError = nullptr;
+  decltype(&ncclCommAbort) CommAbort = nullptr;
+  decltype(&ncclCommDestroy) CommDestroy = nullptr;
+  decltype(&ncclCommFinalize) CommFinalize = nullptr;
+  decltype(&ncclSend) Send = nullptr;
+  decltype(&ncclRecv) Recv = nullptr;
+  decltype(&ncclGroupStart) GroupStart = nullptr;
+  decltype(&ncclGroupEnd) GroupEnd = nullptr;
+  decltype(&ncclGetErrorString) GetErrorString = nullptr;
+  decltype(&ncclGetVersion) GetVersion = nullptr;
+  std::string load_error;
+};
+
+static NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* env = std::getenv("BASALTO_NCCL_LIB");
+    void* h = nullptr;
+    if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // already in the process
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* e = dlerror();
+      api.load_error = e ? e : "dlopen(libnccl.so.2) failed";
+      return;
+    }
+    api.lib = h;
+#define BST_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+    BST_SYM(GetUniqueId, "ncclGetUniqueId");
+    BST_SYM(CommInitRankConfig, "ncclCommInitRankConfig");
+    BST_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+    BST_SYM(CommAbort, "ncclCommAbort");
+    BST_SYM(CommDestroy, "ncclCommDestroy");
+    BST_SYM(CommFinalize, "ncclCommFinalize");
+    BST_SYM(Send, "ncclSend");
+    BST_SYM(Recv, "ncclRecv");
+    BST_SYM(GroupStart, "ncclGroupStart");
+    BST_SYM(GroupEnd, "ncclGroupEnd");
+    BST_SYM(GetErrorString, "ncclGetErrorString");
+    BST_SYM(GetVersion, "ncclGetVersion");
+#undef BST_SYM
+    if (!api.GetUniqueId || !api.CommInitRankConfig || !api.CommGetAsyncError || !api.CommAbort ||
+        !api.CommDestroy || !api.Send || !api.Recv || !api.GroupStart || !api.GroupEnd)
+      api.load_error = "libnccl.so.2 lacks a required symbol";
+  });
+  return api;
+}
+
+static int nccl_ready() {
+  NcclApi& a = nccl();
+  if (!a.load_error.empty()) return fail(BST_ERR_NCCL, "NCCL unavailable: " + a.load_error);
+  return BST_OK;
+}
+
+static int nccl_fail(ncclResult_t r, const char* what) {
+  NcclApi& a = nccl();
+  return fail(BST_ERR_NCCL, std::string(what) + ": " + (a.GetErrorString ? a.GetErrorString(r) : "error"));
+}
+
+}  // namespace bst
+
+using namespace bst;
+
+struct bst_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0, rank = 0, device = 0;
+  double timeout_s = 60.0;
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ev_bnd = nullptr, ev_comm = nullptr;
+};
+
+namespace bst {
+// Poll a non-blocking communicator until its pending operation leaves ncclInProgress.
+static int wait_comm(bst_comm* c, const char* what) {
+  NcclApi& a = nccl();
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclInProgress;
+    ncclResult_t r = a.CommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) return nccl_fail(r, what);
+    if (st == ncclSuccess) return BST_OK;
+    if (st != ncclInProgress) return nccl_fail(st, what);
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > c->timeout_s) return fail(BST_ERR_TIMEOUT, std::string(what) + ": timed out");
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+}  // namespace bst
+
+extern "C" {
+
+int bst_nccl_get_unique_id(uint8_t id_out[128]) {
+  clear_error();
+  if (!id_out) return fail(BST_ERR_INVALID, "null output");
+  int rc = nccl_ready();
+  if (rc) return rc;
+  ncclUniqueId id;
+  ncclResult_t r = nccl().GetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(id_out, &id, 128);
+  return BST_OK;
+}
+
+int bst_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, int32_t device, double timeout_s,
+                    bst_comm** out) {
+  clear_error();
+  if (!id || !out) return fail(BST_ERR_INVALID, "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(BST_ERR_INVALID, "bad rank/nranks");
+  int rc = nccl_ready();
+  if (rc) return rc;
+  BST_CUDA(cudaSetDevice(device));
+  auto* c = new bst_comm();
+  c->nranks = nranks;
+  c->rank = rank;
+  c->device = device;
+  c->timeout_s = timeout_s > 0 ? timeout_s : 60.0;
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, 128);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = nccl().CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    delete c;
+    return nccl_fail(r, "ncclCommInitRankConfig");
+  }
+  rc = wait_comm(c, "NCCL communicator bootstrap");
+  if (rc) {
+    const std::string msg = bst_last_error();
+    if (c->comm) nccl().CommAbort(c->comm);
+    delete c;
+    return fail(rc, msg);
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_bnd, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_comm, cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    nccl().CommAbort(c->comm);
+    delete c;
+    return cuda_fail(e, "comm stream/events");
+  }
+  *out = c;
+  return BST_OK;
+}
+
+static void release_cuda(bst_comm* c) {
+  if (c->ev_bnd) cudaEventDestroy(c->ev_bnd);
+  if (c->ev_comm) cudaEventDestroy(c->ev_comm);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
+}
+
+int bst_comm_destroy(bst_comm* c) {
+  clear_error();
+  if (!c) return BST_OK;
+  int rc = BST_OK;
+  if (c->comm) {
+    cudaSetDevice(c->device);
+    if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
+    if (nccl().CommFinalize) {
+      ncclResult_t r = nccl().CommFinalize(c->comm);
+      if (r == ncclSuccess || r == ncclInProgress) rc = wait_comm(c, "ncclCommFinalize");
+      else rc = nccl_fail(r, "ncclCommFinalize");
+    }
+    if (rc == BST_OK) {
+      ncclResult_t r = nccl().CommDestroy(c->comm);
+      if (r != ncclSuccess) rc = nccl_fail(r, "ncclCommDestroy");
+    } else {
+      nccl().CommAbort(c->comm);
+    }
+  }
+  release_cuda(c);
+  delete c;
+  return rc;
+}
+
+int bst_comm_abort(bst_comm* c) {
+  clear_error();
+  if (!c) return BST_OK;
+  if (c->comm) nccl().CommAbort(c->comm);
+  release_cuda(c);
+  delete c;
+  return BST_OK;
+}
+
+int bst_comm_rank(const bst_comm* c) { return c ? c->rank : -1; }
+int bst_comm_size(const bst_comm* c) { return c ? c->nranks : -1; }
+
+static int halo_enqueue(bst_comm* c, void* slab, int32_t dtype, int64_t plane_elems, int64_t n_local,
+                        int32_t ghost, cudaStream_t st) {
+  if (c->nranks == 1 || ghost == 0) return BST_OK;
+  const size_t es = dtype == BST_F64 ? 8 : 4;
+  const ncclDataType_t nt = dtype == BST_F64 ? ncclFloat64 : ncclFloat32;
+  const size_t count = size_t(ghost) * size_t(plane_elems);
+  char* base = static_cast<char*>(slab);
+  char* lo_ghost = base;
+  char* lo_owned = base + size_t(ghost) * plane_elems * es;
+  char* hi_owned = base + size_t(n_local) * plane_elems * es;
+  char* hi_ghost = base + size_t(n_local + ghost) * plane_elems * es;
+  NcclApi& a = nccl();
+  ncclResult_t r = a.GroupStart();
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGroupStart");
+  ncclResult_t e1 = ncclSuccess, e2 = ncclSuccess, e3 = ncclSuccess, e4 = ncclSuccess;
+  if (c->rank > 0) {
+    e1 = a.Send(lo_owned, count, nt, c->rank - 1, c->comm, st);
+    e2 = a.Recv(lo_ghost, count, nt, c->rank - 1, c->comm, st);
+  }
+  if (c->rank < c->nranks - 1) {
+    e3 = a.Send(hi_owned, count, nt, c->rank + 1, c->comm, st);
+    e4 = a.Recv(hi_ghost, count, nt, c->rank + 1, c->comm, st);
+  }
+  r = a.GroupEnd();
+  for (ncclResult_t e : {e1, e2, e3, e4})
+    if (e != ncclSuccess && e != ncclInProgress) return nccl_fail(e, "ncclSend/ncclRecv");
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclGroupEnd");
+  return wait_comm(c, "halo exchange enqueue");
+}
+
+int bst_halo_exchange(bst_comm* c, void* slab, int32_t dtype, int64_t plane_elems, int64_t n_local, int32_t ghost,
+                      void* stream) {
+  clear_error();
+  if (!c || !slab) return fail(BST_ERR_INVALID, "null argument");
+  if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+  if (plane_elems <= 0 || ghost < 0 || n_local < ghost) return fail(BST_ERR_INVALID, "slab must own at least `ghost` planes");
+  return halo_enqueue(c, slab, dtype, plane_elems, n_local, ghost, static_cast<cudaStream_t>(stream));
+}
+
+int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                    void* a, void* b, int32_t nsteps, void* stream) {
+  clear_error();
+  if (!c || !prog || !local_shape || !a || !b) return fail(BST_ERR_INVALID, "null argument");
+  if (a == b) return fail(BST_ERR_INVALID, "ping-pong slabs must differ");
+  if (nsteps < 0) return fail(BST_ERR_INVALID, "negative step count");
+  if (ndim < 2) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
+  // Canonicalise against the owned extent, then widen axis 0 by the ghost planes.
+  Canon k;
+  int rc = canonicalize(prog, ndim, local_shape, &k);
+  if (rc) return rc;
+  if (k.boundary != BST_BOUNDARY_ZERO) return fail(BST_ERR_INVALID, "slab sweeps need a same-size program");
+  const int R = k.R[0];
+  const int64_t nl = local_shape[0];
+  if (R > 0 && nl < R) return fail(BST_ERR_INVALID, "each rank must own at least `radius` planes");
+  int64_t plane = 1;
+  for (int i = 1; i < ndim; ++i) plane *= local_shape[i];
+  const size_t es = dtype == BST_F64 ? 8 : 4;
+  k.n[0] = nl + 2 * R;  // input includes the ghost planes
+  k.org[0] = R;         // output plane o reads input plane o + R + dm
+  k.no[0] = nl;
+  int64_t st_t[3], s[3];
+  {
+    int64_t acc = 1;
+    for (int i = ndim - 1; i >= 0; --i) {
+      st_t[i] = acc;
+      acc *= (i == 0 ? nl + 2 * R : local_shape[i]);
+    }
+  }
+  logical_strides(ndim, st_t, s);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  BST_CUDA(cudaSetDevice(c->device));
+  char* src = static_cast<char*>(a);
+  char* dst = static_cast<char*>(b);
+  const size_t ghost_bytes = size_t(R) * plane * es;
+  const int64_t lo_end = std::min<int64_t>(R, nl);
+  const int64_t hi_begin = std::max<int64_t>(nl - R, lo_end);
+  for (int step = 0; step < nsteps; ++step) {
+    if (step > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));  // src ghosts have arrived
+    void* out = dst + ghost_bytes;
+    // Boundary planes first: they feed the exchange.
+    rc = launch_sweep(k, dtype, src, s, out, s, 0, lo_end, st);
+    if (!rc && hi_begin < nl) rc = launch_sweep(k, dtype, src, s, out, s, hi_begin, nl, st);
+    if (rc) return rc;
+    if (c->nranks > 1 && R > 0) {
+      BST_CUDA(cudaEventRecord(c->ev_bnd, st));
+      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_bnd, 0));
+      rc = halo_enqueue(c, dst, dtype, plane, nl, R, c->comm_stream);
+      if (rc) return rc;
+      BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
+    } else {
+      BST_CUDA(cudaEventRecord(c->ev_comm, st));
+    }
+    // Interior planes overlap the exchange.
+    if (lo_end < hi_begin) {
+      rc = launch_sweep(k, dtype, src, s, out, s, lo_end, hi_begin, st);
+      if (rc) return rc;
+    }
+    std::swap(src, dst);
+  }
+  if (nsteps > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
+  return BST_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,487 @@
+// bst_interceptor.cu — the C++ interceptor behind basalto._rust.PyBasaltoInterceptor.
+//
+// Mirrors crates/basalto-tree/src/interceptor.rs: validate -> radius from the op name ->
+// device identity -> cache key (crates/basalto-core/src/hasher.rs) -> L1 plan cache
+// (crates/basalto-tree/src/local_cache.rs, an in-memory LRU of capacity 10 000) with a
+// per-key in-flight lock (interceptor.rs:391-396) -> launch.  The "plan" replaces the
+// reference's PTX blob: a validated, canonical stencil program; the kernels themselves
+// are compiled ahead of time for sm_100a.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <list>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "bst_internal.h"
+
+namespace bst {
+
+// ---- BLAKE3 (published algorithm; 7-round compression, 1 KiB chunks, binary tree) ----
+namespace b3 {
+static const uint32_t IV[8] = {0x6A09E667u, 0xBB67AE85u, 0x3C6EF372u, 0xA54FF53Au,
+                               0x510E527Fu, 0x9B05688Cu, 0x1F83D9ABu, 0x5BE0CD19u};
+static const int PERM[16] = {2, 6, 3, 10, 7, 0, 4, 13, 1, 11, 12, 5, 9, 14, 15, 8};
+enum : uint32_t { CHUNK_START = 1, CHUNK_END = 2, PARENT = 4, ROOT = 8, KEYED_HASH = 16 };
+
+static inline uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+static inline void g(uint32_t* s, int a, int b, int c, int d, uint32_t mx, uint32_t my) {
+  s[a] = s[a] + s[b] + mx;
+  s[d] = rotr(s[d] ^ s[a], 16);
+  s[c] = s[c] + s[d];
+  s[b] = rotr(s[b] ^ s[c], 12);
+  s[a] = s[a] + s[b] + my;
+  s[d] = rotr(s[d] ^ s[a], 8);
+  s[c] = s[c] + s[d];
+  s[b] = rotr(s[b] ^ s[c], 7);
+}
+static void compress(const uint32_t cv[8], const uint32_t block[16], uint64_t counter, uint32_t len,
+                     uint32_t flags, uint32_t out[16]) {
+  uint32_t s[16] = {cv[0], cv[1], cv[2], cv[3], cv[4], cv[5], cv[6], cv[7],
+                    IV[0], IV[1], IV[2], IV[3], uint32_t(counter), uint32_t(counter >> 32), len, flags};
+  uint32_t m[16];
+  std::memcpy(m, block, sizeof m);
+  for (int r = 0; r < 7; ++r) {
+    g(s, 0, 4, 8, 12, m[0], m[1]);
+    g(s, 1, 5, 9, 13, m[2], m[3]);
+    g(s, 2, 6, 10, 14, m[4], m[5]);
+    g(s, 3, 7, 11, 15, m[6], m[7]);
+    g(s, 0, 5, 10, 15, m[8], m[9]);
+    g(s, 1, 6, 11, 12, m[10], m[11]);
+    g(s, 2, 7, 8, 13, m[12], m[13]);
+    g(s, 3, 4, 9, 14, m[14], m[15]);
+    uint32_t t[16];
+    for (int i = 0; i < 16; ++i) t[i] = m[PERM[i]];
+    std::memcpy(m, t, sizeof m);
+  }
+  for (int i = 0; i < 8; ++i) {
+    out[i] = s[i] ^ s[i + 8];
+    out[i + 8] = s[i + 8] ^ cv[i];
+  }
+}
+static void load_block(const uint8_t* p, size_t n, uint32_t w[16]) {
+  uint8_t buf[64] = {0};
+  std::memcpy(buf, p, n);
+  for (int i = 0; i < 16; ++i)
+    w[i] = uint32_t(buf[4 * i]) | uint32_t(buf[4 * i + 1]) << 8 | uint32_t(buf[4 * i + 2]) << 16 |
+           uint32_t(buf[4 * i + 3]) << 24;
+}
+// Output node of a chunk or parent before the ROOT decision.
+struct Node {
+  uint32_t cv[8];
+  uint32_t block[16];
+  uint64_t counter;
+  uint32_t len, flags;
+  void chaining(uint32_t out8[8]) const {
+    uint32_t o[16];
+    compress(cv, block, counter, len, flags, o);
+    std::memcpy(out8, o, 32);
+  }
+  void root(uint8_t out32[32]) const {
+    uint32_t o[16];
+    compress(cv, block, 0, len, flags | ROOT, o);
+    for (int i = 0; i < 8; ++i)
+      for (int b = 0; b < 4; ++b) out32[4 * i + b] = uint8_t(o[i] >> (8 * b));
+  }
+};
+static Node chunk_node(const uint32_t key[8], const uint8_t* p, size_t n, uint64_t chunk, uint32_t base) {
+  uint32_t cv[8];
+  std::memcpy(cv, key, 32);
+  const size_t nblocks = n == 0 ? 1 : (n + 63) / 64;
+  Node last{};
+  for (size_t b = 0; b < nblocks; ++b) {
+    const size_t off = b * 64, len = n - off < 64 ? n - off : 64;
+    uint32_t w[16];
+    load_block(p + off, n == 0 ? 0 : len, w);
+    uint32_t flags = base | (b == 0 ? CHUNK_START : 0) | (b + 1 == nblocks ? CHUNK_END : 0);
+    if (b + 1 == nblocks) {
+      std::memcpy(last.cv, cv, 32);
+      std::memcpy(last.block, w, 64);
+      last.counter = chunk;
+      last.len = uint32_t(n == 0 ? 0 : len);
+      last.flags = flags;
+    } else {
+      uint32_t o[16];
+      compress(cv, w, chunk, 64, flags, o);
+      std::memcpy(cv, o, 32);
+    }
+  }
+  return last;
+}
+static Node parent_node(const uint32_t key[8], const uint32_t l[8], const uint32_t r[8], uint32_t base) {
+  Node nd{};
+  std::memcpy(nd.cv, key, 32);
+  std::memcpy(nd.block, l, 32);
+  std::memcpy(nd.block + 8, r, 32);
+  nd.counter = 0;
+  nd.len = 64;
+  nd.flags = base | PARENT;
+  return nd;
+}
+// Hash of the subtree over chunks [c0, c0 + nchunks) (left subtree = largest power of two).
+static Node subtree(const uint32_t key[8], const uint8_t* p, size_t n, uint64_t c0, uint32_t base) {
+  const size_t nchunks = n <= 1024 ? 1 : (n + 1023) / 1024;
+  if (nchunks == 1) return chunk_node(key, p, n, c0, base);
+  size_t left = 1;
+  while (left * 2 < nchunks) left *= 2;
+  const size_t lbytes = left * 1024;
+  uint32_t lcv[8], rcv[8];
+  subtree(key, p, lbytes, c0, base).chaining(lcv);
+  subtree(key, p + lbytes, n - lbytes, c0 + left, base).chaining(rcv);
+  return parent_node(key, lcv, rcv, base);
+}
+static void hash(const uint8_t* p, size_t n, const uint8_t* key32, uint8_t out[32]) {
+  uint32_t key[8];
+  uint32_t base = 0;
+  if (key32) {
+    for (int i = 0; i < 8; ++i)
+      key[i] = uint32_t(key32[4 * i]) | uint32_t(key32[4 * i + 1]) << 8 | uint32_t(key32[4 * i + 2]) << 16 |
+               uint32_t(key32[4 * i + 3]) << 24;
+    base = KEYED_HASH;
+  } else {
+    std::memcpy(key, IV, 32);
+  }
+  subtree(key, p, n, 0, base).root(out);
+}
+}  // namespace b3
+
+// ---- hasher.rs serialization ------------------------------------------------------
+static void put_fixed(std::vector<uint8_t>& b, const char* s, size_t width) {
+  const size_t n = s ? std::min(std::strlen(s), width) : 0;
+  const size_t at = b.size();
+  b.resize(at + width, 0);
+  if (n) std::memcpy(b.data() + at, s, n);
+}
+template <typename I>
+static void put_le(std::vector<uint8_t>& b, I v) {
+  for (size_t i = 0; i < sizeof(I); ++i) b.push_back(uint8_t(uint64_t(v) >> (8 * i)));
+}
+
+static std::string to_hex(const uint8_t* d, size_t n) {
+  static const char* hx = "0123456789abcdef";
+  std::string s(2 * n, '0');
+  for (size_t i = 0; i < n; ++i) {
+    s[2 * i] = hx[d[i] >> 4];
+    s[2 * i + 1] = hx[d[i] & 15];
+  }
+  return s;
+}
+
+static std::vector<uint8_t> serialize_key(const char* op, const char* dtype, int ndim, const int64_t* shape,
+                                          const int64_t* strides, int64_t radius, const bst_device_caps* caps) {
+  std::vector<uint8_t> b;
+  put_fixed(b, op, 32);
+  put_fixed(b, dtype, 16);
+  put_le<uint64_t>(b, uint64_t(ndim));
+  for (int i = 0; i < ndim; ++i) put_le<uint64_t>(b, uint64_t(shape[i]));
+  put_le<uint64_t>(b, uint64_t(ndim));
+  for (int i = 0; i < ndim; ++i) put_le<int64_t>(b, strides ? strides[i] : 0);
+  put_le<uint64_t>(b, uint64_t(radius));
+  b.push_back(0);  // no matmul fields on the stencil path
+  put_fixed(b, caps ? caps->vendor : "unknown", 16);
+  put_fixed(b, caps ? caps->arch : "generic", 16);
+  put_fixed(b, caps ? caps->driver : "unknown", 32);
+  if (caps) {
+    put_le<int32_t>(b, caps->compute_capability_major);
+    put_le<int32_t>(b, caps->compute_capability_minor);
+    put_le<int32_t>(b, caps->max_threads_per_block);
+    put_le<uint64_t>(b, caps->max_shared_memory_per_block);
+    put_le<int32_t>(b, caps->max_registers_per_block);
+    put_le<int32_t>(b, caps->warp_size);
+    put_le<int32_t>(b, caps->multi_processor_count);
+  } else {
+    b.resize(b.size() + 7 * 8, 0);
+  }
+  return b;
+}
+
+// ---- plan cache ---------------------------------------------------------------------
+struct Plan {
+  Canon canon;
+  int dtype = BST_F32;
+  int ndim = 0;
+  std::vector<int64_t> shape, strides;
+};
+
+class LruCache {
+ public:
+  explicit LruCache(size_t cap) : cap_(cap) {}
+  std::shared_ptr<Plan> get(const std::string& k) {
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = map_.find(k);
+    if (it == map_.end()) return nullptr;
+    order_.splice(order_.begin(), order_, it->second.second);
+    return it->second.first;
+  }
+  void put(const std::string& k, std::shared_ptr<Plan> p) {
+    std::lock_guard<std::mutex> lk(mu_);
+    auto it = map_.find(k);
+    if (it != map_.end()) {
+      it->second.first = std::move(p);
+      order_.splice(order_.begin(), order_, it->second.second);
+      return;
+    }
+    order_.push_front(k);
+    map_.emplace(k, std::make_pair(std::move(p), order_.begin()));
+    while (map_.size() > cap_) {
+      map_.erase(order_.back());
+      order_.pop_back();
+    }
+  }
+  size_t size() const {
+    std::lock_guard<std::mutex> lk(mu_);
+    return map_.size();
+  }
+
+ private:
+  size_t cap_;
+  mutable std::mutex mu_;
+  std::list<std::string> order_;
+  std::unordered_map<std::string, std::pair<std::shared_ptr<Plan>, std::list<std::string>::iterator>> map_;
+};
+
+static bool read_secret_key(uint8_t key[32]) {
+  const char* env = std::getenv("BASALTO_SECRET_KEY_FILE");
+  const char* path = env && *env ? env : "/etc/basalto/secret.key";
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  f.read(reinterpret_cast<char*>(key), 32);
+  return f.gcount() == 32;
+}
+
+static int parse_dtype(const char* s) {
+  if (!s) return -1;
+  if (!std::strcmp(s, "float32") || !std::strcmp(s, "f32")) return BST_F32;
+  if (!std::strcmp(s, "float64") || !std::strcmp(s, "f64")) return BST_F64;
+  return -1;
+}
+
+static void fill_driver_string(bst_device_caps* c) {
+  std::snprintf(c->vendor, sizeof c->vendor, "%s", "nvidia");
+  std::snprintf(c->driver, sizeof c->driver, "%s", "unknown");
+  std::ifstream f("/proc/driver/nvidia/version");
+  std::string line;
+  while (std::getline(f, line)) {
+    if (line.find("NVRM version") == std::string::npos) continue;
+    // Third whitespace-separated field, as hardware.rs:154-159.
+    size_t pos = 0;
+    std::string tok[3];
+    for (int i = 0; i < 3; ++i) {
+      while (pos < line.size() && std::isspace((unsigned char)line[pos])) ++pos;
+      size_t e = pos;
+      while (e < line.size() && !std::isspace((unsigned char)line[e])) ++e;
+      tok[i] = line.substr(pos, e - pos);
+      pos = e;
+    }
+    if (!tok[2].empty()) std::snprintf(c->driver, sizeof c->driver, "%s", tok[2].c_str());
+    break;
+  }
+}
+
+}  // namespace bst
+
+using namespace bst;
+
+struct bst_interceptor {
+  LruCache cache{10000};
+  std::mutex inflight_mu;
+  std::unordered_map<std::string, std::shared_ptr<std::mutex>> inflight;
+  std::atomic<int64_t> hits{0};
+  std::mutex key_mu;
+  std::string last_key;
+  uint8_t secret[32] = {0};
+  bool have_secret = false;
+  std::mutex caps_mu;
+  std::unordered_map<int, bst_device_caps> caps;
+};
+
+extern "C" {
+
+int bst_blake3(const uint8_t* data, int64_t len, const uint8_t* key32, uint8_t* out32) {
+  clear_error();
+  if (!out32 || (len > 0 && !data) || len < 0) return fail(BST_ERR_INVALID, "bad blake3 arguments");
+  b3::hash(data, size_t(len), key32, out32);
+  return BST_OK;
+}
+
+int bst_cache_key(const char* op, const char* dtype, int32_t ndim, const int64_t* shape, const int64_t* strides,
+                  int64_t radius, const bst_device_caps* caps, const uint8_t* extra, int64_t extra_len,
+                  const uint8_t* key32, char* hex_out) {
+  clear_error();
+  if (!hex_out || (ndim > 0 && !shape) || ndim < 0 || extra_len < 0) return fail(BST_ERR_INVALID, "bad cache-key arguments");
+  std::vector<uint8_t> b = serialize_key(op, dtype, ndim, shape, strides, radius, caps);
+  if (extra && extra_len) b.insert(b.end(), extra, extra + extra_len);
+  uint8_t zero[32] = {0}, d[32];
+  b3::hash(b.data(), b.size(), key32 ? key32 : zero, d);
+  std::memcpy(hex_out, to_hex(d, 32).c_str(), 65);
+  return BST_OK;
+}
+
+int bst_interceptor_create(bst_interceptor** out) {
+  clear_error();
+  if (!out) return fail(BST_ERR_INVALID, "null output handle");
+  auto* h = new (std::nothrow) bst_interceptor();
+  if (!h) return fail(BST_ERR_INVALID, "out of host memory");
+  h->have_secret = read_secret_key(h->secret);
+  *out = h;
+  return BST_OK;
+}
+
+void bst_interceptor_destroy(bst_interceptor* h) { delete h; }
+
+int64_t bst_interceptor_cache_size(const bst_interceptor* h) { return h ? int64_t(h->cache.size()) : 0; }
+int64_t bst_interceptor_cache_hits(const bst_interceptor* h) { return h ? h->hits.load() : 0; }
+
+int bst_interceptor_last_key(const bst_interceptor* h, char* hex_out) {
+  if (!h || !hex_out) return fail(BST_ERR_INVALID, "null argument");
+  auto* hh = const_cast<bst_interceptor*>(h);
+  std::lock_guard<std::mutex> lk(hh->key_mu);
+  std::snprintf(hex_out, 65, "%s", h->last_key.c_str());
+  return BST_OK;
+}
+
+int bst_interceptor_compile_and_execute(bst_interceptor* h, const char* op, const char* dtype, int32_t ndim,
+                                        const int64_t* shape, const int64_t* strides, const char* job_id,
+                                        uint64_t device_ptr_x, uint64_t device_ptr_y, uint64_t device_ptr_z,
+                                        const double* custom_coeffs, int64_t ncoeffs, const bst_program* program,
+                                        void* stream) {
+  (void)job_id;        // recorded by the caller; not part of the key (interceptor.rs:349)
+  (void)device_ptr_z;  // unused on the stencil path (python/basalto/compiler.py:93)
+  clear_error();
+  if (!h) return fail(BST_ERR_INVALID, "null interceptor");
+  if (!op) return fail(BST_ERR_INVALID, "null op");
+  if (std::strncmp(op, "matmul", 6) == 0)
+    return fail(BST_ERR_UNSUPPORTED, "matmul ops are outside the stencil path of this build");
+  if (ndim < 1 || ndim > 3)
+    return fail(BST_ERR_INVALID, "only 1-D, 2-D and 3-D are supported (ndim = " + std::to_string(ndim) + ")");
+  if (!shape || !strides) return fail(BST_ERR_INVALID, "shape and strides must have the same length");
+  if (device_ptr_x == 0 || device_ptr_y == 0) return fail(BST_ERR_INVALID, "null device pointers");
+  const int dt = parse_dtype(dtype);
+  if (dt < 0) return fail(BST_ERR_UNSUPPORTED, std::string("unsupported dtype '") + (dtype ? dtype : "") + "'");
+
+  const int32_t radius = bst_extract_radius(op);
+  int dev = 0;
+  BST_CUDA(cudaGetDevice(&dev));
+  bst_device_caps caps{};
+  {
+    std::lock_guard<std::mutex> lk(h->caps_mu);
+    auto it = h->caps.find(dev);
+    if (it == h->caps.end()) {
+      int rc = bst_device_caps_query(dev, &caps);
+      if (rc) return rc;
+      fill_driver_string(&caps);
+      h->caps[dev] = caps;
+    } else {
+      caps = it->second;
+    }
+  }
+  // Program / coefficient digest appended to the reference's key material.
+  std::vector<uint8_t> extra;
+  if (program) {
+    // Digest only the populated part of the descriptor.
+    std::vector<uint8_t> pb;
+    put_le<int32_t>(pb, program->ndim);
+    put_le<int32_t>(pb, program->ntaps);
+    put_le<int32_t>(pb, program->nterms);
+    put_le<int32_t>(pb, program->init_zero);
+    put_le<int32_t>(pb, program->boundary);
+    for (int i = 0; i < 3; ++i) put_le<int64_t>(pb, program->out_shape[i]);
+    const int nt = std::max(0, std::min(program->ntaps, BST_MAX_TAPS));
+    const int ng = std::max(0, std::min(program->nterms, BST_MAX_TERMS));
+    for (int i = 0; i < nt; ++i)
+      for (int a = 0; a < 3; ++a) put_le<int32_t>(pb, program->tap[i][a]);
+    for (int g = 0; g < ng; ++g) {
+      put_le<int32_t>(pb, program->term_first[g]);
+      put_le<int32_t>(pb, program->term_count[g]);
+      put_le<int32_t>(pb, program->term_op[g]);
+      uint64_t bits;
+      std::memcpy(&bits, &program->term_scale[g], 8);
+      put_le<uint64_t>(pb, bits);
+    }
+    uint8_t d[32];
+    b3::hash(pb.data(), pb.size(), nullptr, d);
+    extra.push_back('P');
+    extra.insert(extra.end(), d, d + 32);
+  } else if (custom_coeffs && ncoeffs > 0) {
+    uint8_t d[32];
+    b3::hash(reinterpret_cast<const uint8_t*>(custom_coeffs), size_t(ncoeffs) * sizeof(double), nullptr, d);
+    extra.push_back('C');
+    extra.insert(extra.end(), d, d + 32);
+  }
+  char key[65];
+  int rc = bst_cache_key(op, dtype, ndim, shape, strides, radius, &caps, extra.data(), int64_t(extra.size()),
+                         h->have_secret ? h->secret : nullptr, key);
+  if (rc) return rc;
+  const std::string skey(key);
+  {
+    std::lock_guard<std::mutex> lk(h->key_mu);
+    h->last_key = skey;
+  }
+
+  std::shared_ptr<Plan> plan = h->cache.get(skey);
+  if (plan) {
+    h->hits.fetch_add(1);
+  } else {
+    std::shared_ptr<std::mutex> lock;
+    {
+      std::lock_guard<std::mutex> lk(h->inflight_mu);
+      auto& slot = h->inflight[skey];
+      if (!slot) slot = std::make_shared<std::mutex>();
+      lock = slot;
+    }
+    std::lock_guard<std::mutex> build_lk(*lock);
+    plan = h->cache.get(skey);  // filled by another thread while we waited
+    if (plan) {
+      h->hits.fetch_add(1);
+    } else {
+      auto p = std::make_shared<Plan>();
+      std::unique_ptr<bst_program> box;
+      const bst_program* prog = program;
+      if (!prog) {
+        box.reset(new bst_program);
+        rc = bst_program_box(ndim, radius, custom_coeffs, custom_coeffs ? ncoeffs : 0, box.get());
+        if (rc) return rc;
+        prog = box.get();
+      }
+      rc = canonicalize(prog, ndim, shape, &p->canon);
+      if (rc) return rc;
+      p->dtype = dt;
+      p->ndim = ndim;
+      p->shape.assign(shape, shape + ndim);
+      p->strides.assign(strides, strides + ndim);
+      h->cache.put(skey, p);
+      plan = p;
+    }
+    std::lock_guard<std::mutex> lk(h->inflight_mu);
+    h->inflight.erase(skey);
+  }
+
+  // y has x's strides for same-size programs (y = zeros_like(x), compiler.py:78) and is
+  // C-contiguous for valid-region programs.
+  const Canon& c = plan->canon;
+  int64_t xs[3], ys[3], ys_t[3];
+  logical_strides(ndim, strides, xs);
+  if (c.boundary == BST_BOUNDARY_ZERO) {
+    std::copy(strides, strides + ndim, ys_t);
+  } else {
+    int64_t s = 1;
+    for (int i = ndim - 1; i >= 0; --i) {
+      ys_t[i] = s;
+      s *= program->out_shape[i];
+    }
+  }
+  logical_strides(ndim, ys_t, ys);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = launch_sweep(c, plan->dtype, reinterpret_cast<const void*>(device_ptr_x), xs,
+                    reinterpret_cast<void*>(device_ptr_y), ys, 0, c.no[0], st);
+  if (rc) return rc;
+  if (!stream) BST_CUDA(cudaStreamSynchronize(st));  // synchronous like the reference's launch
+  return BST_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// bst_internal.h — host-side internals shared by the C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/basalto_b200.h"
+#include "bst_types.cuh"
+
+namespace bst {
+
+// ---- error reporting --------------------------------------------------------------
+void set_error(const std::string& msg);
+void clear_error();
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+#define BST_CUDA(call)                                  \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return ::bst::cuda_fail(e_, #call); \
+  } while (0)
+
+extern std::atomic<uint64_t> g_launches;
+
+// ---- canonical program in logical [M, Y, X] space ----------------------------------
+struct Canon {
+  int ndim = 0;
+  int boundary = BST_BOUNDARY_ZERO;
+  int init_zero = 0;
+  int ntaps = 0, nterms = 0;
+  std::vector<Tap> taps;       // centred offsets (input = output + org + tap)
+  std::vector<Term> terms;
+  std::vector<double> scale;
+  int R[3] = {0, 0, 0};    // per logical axis: max |tap|
+  int org[3] = {0, 0, 0};  // output -> input origin shift
+  int64_t n[3] = {1, 1, 1};   // input extents
+  int64_t no[3] = {1, 1, 1};  // output extents
+};
+
+// Validate `p` against an input of `shape` (ndim entries) and fill `c`.
+int canonicalize(const bst_program* p, int ndim, const int64_t* shape, Canon* c);
+
+// Logical strides [M, Y, X] from torch-order strides (elements).
+void logical_strides(int ndim, const int64_t* strides, int64_t out[3]);
+
+// Launch one sweep.  x/y strides are logical [M,Y,X]; m range is in output planes.
+// `slab_ghost` > 0 marks an input whose axis-0 ghosts are physically present.
+int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
+                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st);
+
+// Device error word (kernels OR bits into it); allocated once per device.
+unsigned* device_error_word();
+// Reads and clears the calling device's error word (synchronizes the stream).
+int check_device_error(cudaStream_t st);
+
+}  // namespace bst

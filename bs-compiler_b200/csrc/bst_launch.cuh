@@ -1,0 +1,232 @@
+// bst_launch.cuh — typed launchers for one catalog shape (included by the per-dtype
+// instantiation units).
+#pragma once
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "bst_internal.h"
+#include "bst_kernels.cuh"
+
+namespace bst {
+
+struct LaunchReq {
+  const Canon* c;
+  const void* x;
+  int64_t xs[3];
+  void* y;
+  int64_t ys[3];
+  int64_t m_lo, m_hi;
+  cudaStream_t st;
+};
+
+template <typename T, int N>
+Coefs<T, N> make_coefs(const Canon& c) {
+  Coefs<T, N> k{};
+  for (int g = 0; g < c.nterms && g < N; ++g) k.scale[g] = T(c.scale[g]);
+  k.init_zero = c.init_zero;
+  return k;
+}
+
+inline GridDesc make_grid(const LaunchReq& r) {
+  GridDesc g{};
+  for (int i = 0; i < 3; ++i) {
+    g.n[i] = r.c->n[i];
+    g.s[i] = r.xs[i];
+    g.no[i] = r.c->no[i];
+    g.so[i] = r.ys[i];
+    g.org[i] = r.c->org[i];
+  }
+  g.m_lo = r.m_lo;
+  g.m_hi = r.m_hi;
+  return g;
+}
+
+int sm_count();
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+
+// ---- direct ---------------------------------------------------------------------
+template <typename T, class S>
+int launch_direct(const LaunchReq& r) {
+  const GridDesc g = make_grid(r);
+  const long long total = (r.m_hi - r.m_lo) * g.no[1] * g.no[2];
+  if (total <= 0) return BST_OK;
+  long long blocks = (total + 255) / 256;
+  const long long cap = (long long)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  direct_kernel<T, S><<<unsigned(blocks), 256, 0, r.st>>>(static_cast<const T*>(r.x),
+                                                         static_cast<T*>(r.y), g, make_coefs<T, S::NTERMS>(*r.c));
+  BST_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+template <typename T>
+int launch_direct_table(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  const GridDesc g = make_grid(r);
+  const long long total = (r.m_hi - r.m_lo) * g.no[1] * g.no[2];
+  if (total <= 0) return BST_OK;
+  // The table and scales travel in one stream-ordered device buffer.
+  struct Blob {
+    TableProgram p;
+    T scale[kMaxTerms];
+  };
+  std::vector<unsigned char> host(sizeof(Blob), 0);
+  Blob* h = reinterpret_cast<Blob*>(host.data());
+  h->p.ntaps = c.ntaps;
+  h->p.nterms = c.nterms;
+  h->p.init_zero = c.init_zero;
+  for (int i = 0; i < c.ntaps; ++i) {
+    h->p.tap[i][0] = short(c.taps[i].dm);
+    h->p.tap[i][1] = short(c.taps[i].dy);
+    h->p.tap[i][2] = short(c.taps[i].dx);
+  }
+  for (int i = 0; i < c.nterms; ++i) {
+    h->p.term_first[i] = short(c.terms[i].first);
+    h->p.term_count[i] = short(c.terms[i].count);
+    h->p.term_op[i] = (unsigned char)c.terms[i].op;
+    h->scale[i] = T(c.scale[i]);
+  }
+  void* d = nullptr;
+  BST_CUDA(cudaMallocAsync(&d, sizeof(Blob), r.st));
+  cudaError_t e = cudaMemcpyAsync(d, h, sizeof(Blob), cudaMemcpyHostToDevice, r.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(r.st);  // host staging buffer dies on return
+  if (e != cudaSuccess) {
+    cudaFreeAsync(d, r.st);
+    return cuda_fail(e, "upload of the stencil table");
+  }
+  const Blob* db = static_cast<const Blob*>(d);
+  long long blocks = (total + 255) / 256;
+  const long long cap = (long long)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  direct_table_kernel<T><<<unsigned(blocks), 256, 0, r.st>>>(
+      static_cast<const T*>(r.x), static_cast<T*>(r.y), g, &db->p, TableCoefs<T>{db->scale, c.init_zero});
+  e = cudaGetLastError();
+  cudaFreeAsync(d, r.st);
+  if (e != cudaSuccess) return cuda_fail(e, "direct_table_kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+// ---- 1-D line ---------------------------------------------------------------------
+template <typename T, class S, int ORG>
+int launch_line(const LaunchReq& r) {
+  constexpr int V = Vec16<T>::N;
+  LineArgs a{r.c->n[2], r.c->no[2]};
+  const long long nvec = (a.n_out + V - 1) / V;
+  if (nvec <= 0) return BST_OK;
+  long long blocks = (nvec + 255) / 256;
+  const long long cap = (long long)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  line_kernel<T, S, ORG><<<unsigned(blocks), 256, 0, r.st>>>(
+      static_cast<const T*>(r.x), static_cast<T*>(r.y), a, make_coefs<T, S::NTERMS>(*r.c));
+  BST_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+// ---- TMA march ----------------------------------------------------------------------
+template <typename T>
+constexpr CUtensorMapDataType tma_dtype() {
+  return sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT64;
+}
+
+// Whether the request meets TMA's rules for this configuration.
+template <typename T, class C>
+bool march_eligible(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  if (reinterpret_cast<uintptr_t>(r.x) % 16 != 0) return false;
+  if (r.xs[2] != 1) return false;
+  if ((r.xs[1] * E) % 16 != 0 || (r.xs[0] * E) % 16 != 0) return false;
+  if (r.xs[0] <= 0 || r.xs[1] <= 0) return false;
+  for (int i = 0; i < 3; ++i)
+    if (c.n[i] >= (int64_t(1) << 31) || c.no[i] >= (int64_t(1) << 31)) return false;
+  // The tile's first loaded column must sit on a 16-byte boundary.
+  if (((c.org[2] - C::XC) % C::V16 + C::V16) % C::V16 != 0) return false;
+  if (c.R[0] > C::RM || c.R[1] > C::RY || c.R[2] > C::RX) return false;
+  return true;
+}
+
+struct OccKey {
+  const void* fn;
+  int smem;
+  bool operator==(const OccKey& o) const { return fn == o.fn && smem == o.smem; }
+};
+struct OccHash {
+  size_t operator()(const OccKey& k) const { return std::hash<const void*>()(k.fn) ^ size_t(k.smem); }
+};
+int occupancy(const void* fn, int threads, int smem);
+
+// Choose the M-chunk so that equal-size items fill whole waves of resident CTAs.
+inline void choose_chunks(long long base_tiles, long long nm, int rb, int overhead, long long resident,
+                          int* chunk_out, long long* nchunks_out) {
+  double best = 1e300;
+  int best_chunk = int(nm);
+  long long best_n = 1;
+  const long long max_nc = nm / rb + 1;
+  for (long long nc = 1; nc <= max_nc && nc <= 4096; ++nc) {
+    long long chunk = (nm + nc - 1) / nc;
+    chunk = (chunk + rb - 1) / rb * rb;
+    const long long real = (nm + chunk - 1) / chunk;
+    const long long items = base_tiles * real;
+    const long long waves = (items + resident - 1) / resident;
+    const double t = double(waves) * double(chunk + overhead);
+    if (t < best * 0.999) {
+      best = t;
+      best_chunk = int(chunk);
+      best_n = real;
+    }
+  }
+  *chunk_out = best_chunk;
+  *nchunks_out = best_n;
+}
+
+template <typename T, class C>
+int launch_march(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  const long long nm = r.m_hi - r.m_lo;
+  if (nm <= 0) return BST_OK;
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {cuuint64_t(c.n[2]), cuuint64_t(c.n[1]), cuuint64_t(c.n[0])};
+  // Stride of the unit Y axis of a 2-D grid is irrelevant but must be legal.
+  const int64_t sy = c.n[1] == 1 ? r.xs[0] : r.xs[1];
+  const cuuint64_t strides[2] = {cuuint64_t(sy * E), cuuint64_t(r.xs[0] * E)};
+  const cuuint32_t box[3] = {cuuint32_t(C::TXL), cuuint32_t(C::TYL), cuuint32_t(C::RB)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  CUresult cr = enc(&map, tma_dtype<T>(), 3, const_cast<void*>(r.x), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(cr)) + ")");
+
+  auto kern = march_tma_kernel<T, C>;
+
+  MarchArgs a{};
+  a.g = make_grid(r);
+  a.tiles_x = int((c.no[2] + C::TX - 1) / C::TX);
+  a.tiles_y = int((c.no[1] + C::TY - 1) / C::TY);
+  const int occ = occupancy(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
+  if (occ <= 0) return fail(BST_ERR_CUDA, "march kernel does not fit on an SM");
+  const long long resident = (long long)occ * sm_count();
+  long long nchunks = 1;
+  choose_chunks((long long)a.tiles_x * a.tiles_y, nm, C::RB, 2 * C::RM + 2 * C::RB + 8, resident,
+                &a.chunk, &nchunks);
+  a.n_chunks = int(nchunks);
+  a.n_items = (long long)a.tiles_x * a.tiles_y * nchunks;
+  a.err = device_error_word();
+  if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
+  const long long grid = a.n_items < resident ? a.n_items : resident;
+  dim3 block(C::TX, C::NTY);
+  kern<<<unsigned(grid), block, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
+                                                  make_coefs<T, C::shape::NTERMS>(c));
+  BST_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+}  // namespace bst

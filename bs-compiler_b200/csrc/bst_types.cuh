@@ -1,0 +1,73 @@
+// bst_types.cuh — shared device/host types for the stencil kernels.
+//
+// A grid is addressed as three logical axes [M, Y, X] (slowest to fastest):
+//   1-D input [n]        -> [1, 1, n]
+//   2-D input [ny, nx]   -> [ny, 1, nx]   (the row axis is the marching axis M)
+//   3-D input [nz,ny,nx] -> [nz, ny, nx]  (Z is the marching axis M)
+// so one kernel family covers 2-D and 3-D; tap offsets are remapped the same way.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace bst {
+
+constexpr int kMaxTaps = 2304;
+constexpr int kMaxTerms = 2304;
+
+enum TermOp : int { kSum = 0, kMul = 1, kDiv = 2 };
+
+struct Tap {
+  int dm, dy, dx;
+};
+struct Term {
+  int first, count, op;
+};
+
+// Geometry of one launch.  Input coordinate of a tap = output coordinate + org + tap.
+struct GridDesc {
+  int64_t n[3];      // input extents [M, Y, X]
+  int64_t s[3];      // input strides (elements)
+  int64_t no[3];     // output extents
+  int64_t so[3];     // output strides (elements)
+  int32_t org[3];    // output->input origin shift
+  int32_t pad;
+  int64_t m_lo, m_hi;  // output M range computed by this launch
+};
+
+// Runtime scalars of a program (compile-time structure lives in the shape type);
+// passed by value, sized exactly to the shape's term count.
+template <typename T, int N>
+struct Coefs {
+  T scale[N];
+  int init_zero;
+};
+
+// Runtime-table program for the generic kernels (lives in device memory).
+struct TableProgram {
+  int ntaps, nterms, init_zero, pad;
+  short tap[kMaxTaps][3];
+  short term_first[kMaxTerms], term_count[kMaxTerms];
+  unsigned char term_op[kMaxTerms];
+};
+// Scales of a runtime-table program (device memory, element type T).
+template <typename T>
+struct TableCoefs {
+  const T* scale;
+  int init_zero;
+};
+
+// ---- correctly rounded scalar arithmetic, never contracted into FMA -------------
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(a, b); }
+
+template <typename T>
+__device__ __forceinline__ T apply_op(int op, T scale, T s) {
+  // torch: `c * t` and `t * c` are the same IEEE product; `t / c` is IEEE division.
+  return op == kMul ? mul_rn(scale, s) : (op == kDiv ? div_rn(s, scale) : s);
+}
+
+}  // namespace bst
