@@ -291,7 +291,7 @@ def run_basalto(args):
 
     # ---- e2e through the plugin path with host buffers ------------------------------------
     e2e = None
-    if ws == 1:
+    if ws == 1 and args.e2e_steps > 0:
         host_in = w.make_input().pin_memory() if args.host_input else torch.empty(w.shape, dtype=w.dtype).pin_memory()
         host_out = torch.empty(w.shape, dtype=w.dtype).pin_memory()
         torch._dynamo.reset()

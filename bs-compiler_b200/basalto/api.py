@@ -32,6 +32,8 @@ def apply(prog: StencilProgram, x: torch.Tensor, out: torch.Tensor | None = None
         out = torch.empty(oshape, dtype=x.dtype, device=x.device)
     elif tuple(out.shape) != oshape or out.dtype != x.dtype or out.device != x.device:
         raise ValueError("out has the wrong shape, dtype or device")
+    if out.numel() == 0:
+        return out
     cp = prog.to_c(x.shape)
     with torch.cuda.device(x.device):
         _abi.check(_abi.lib().bst_stencil_apply(

@@ -44,14 +44,6 @@ int run_march_or_direct(const LaunchReq& r) {
   return launch_direct<T, typename C::shape>(r);
 }
 
-// Zero-boundary (XC = halo rounded to 16 B) and valid-region (XC = RX) variants.
-template <typename T, class CZ, class CV>
-int run_march2(const LaunchReq& r) {
-  if (march_eligible<T, CZ>(r)) return launch_march<T, CZ>(r);
-  if (march_eligible<T, CV>(r)) return launch_march<T, CV>(r);
-  return launch_direct<T, typename CZ::shape>(r);
-}
-
 template <typename T, class S>
 int run_line(const LaunchReq& r) {
   const Canon& c = *r.c;
@@ -64,11 +56,15 @@ int run_line(const LaunchReq& r) {
   return launch_direct<T, S>(r);
 }
 
-// Tile configurations.  f32 rows of 64/128 columns, f64 rows of 32/64 columns (256 B+).
-template <typename T, class S, int XC>
-using Cfg2D = MarchCfg<T, S, (sizeof(T) == 4 ? 128 : 64), 1, (sizeof(T) == 4 ? 2 : 4), 16, 3, XC>;
-template <typename T, class S, int XC, int NSX>
-using Cfg3D = MarchCfg<T, S, (sizeof(T) == 4 ? 64 : 32), 16, (sizeof(T) == 4 ? 4 : 8), 1, NSX, XC>;
+// Tile configurations.  A tile row is one warp of 16-byte vectors: 128 fp32 or 64 fp64
+// columns.  2-D grids march along rows with one-warp CTAs (many resident per SM);
+// 3-D tiles stack PY-row groups of warps and march along Z.
+template <typename T>
+constexpr int kRowCols = 32 * (16 / int(sizeof(T)));
+template <typename T, class S>
+using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, 4, 2>;
+template <typename T, class S, int TY, int PY, int NSX>
+using Cfg3D = MarchCfg<T, S, kRowCols<T>, TY, PY, 1, NSX>;
 
 template <typename T>
 int dispatch_sweep(const LaunchReq& r) {
@@ -83,32 +79,21 @@ int dispatch_sweep(const LaunchReq& r) {
     return launch_direct_table<T>(r);
   }
   if (c.ndim == 2) {
-    if (shape_matches<Jacobi2D>(c))
-      return run_march_or_direct<T, Cfg2D<T, Jacobi2D, xhalo<T, 1>()>>(r);
-    if (shape_matches<Box<1, 5, false>>(c))
-      return run_march_or_direct<T, Cfg2D<T, Box<1, 5, false>, xhalo<T, 1>()>>(r);
-    if (shape_matches<Box<2, 5, false>>(c))
-      return run_march_or_direct<T, Cfg2D<T, Box<2, 5, false>, xhalo<T, 2>()>>(r);
-    if (shape_matches<Box<3, 5, false>>(c))
-      return run_march_or_direct<T, Cfg2D<T, Box<3, 5, false>, xhalo<T, 3>()>>(r);
-    if (shape_matches<Box<4, 5, false>>(c))
-      return run_march_or_direct<T, Cfg2D<T, Box<4, 5, false>, xhalo<T, 4>()>>(r);
-    if (shape_matches<Box<1, 5, true>>(c))
-      return run_march_or_direct<T, Cfg2D<T, Box<1, 5, true>, xhalo<T, 1>()>>(r);
+    if (shape_matches<Jacobi2D>(c)) return run_march_or_direct<T, Cfg2D<T, Jacobi2D>>(r);
+    if (shape_matches<Box<1, 5, false>>(c)) return run_march_or_direct<T, Cfg2D<T, Box<1, 5, false>>>(r);
+    if (shape_matches<Box<2, 5, false>>(c)) return run_march_or_direct<T, Cfg2D<T, Box<2, 5, false>>>(r);
+    if (shape_matches<Box<3, 5, false>>(c)) return run_march_or_direct<T, Cfg2D<T, Box<3, 5, false>>>(r);
+    if (shape_matches<Box<4, 5, false>>(c)) return run_march_or_direct<T, Cfg2D<T, Box<4, 5, false>>>(r);
+    if (shape_matches<Box<1, 5, true>>(c)) return run_march_or_direct<T, Cfg2D<T, Box<1, 5, true>>>(r);
     return launch_direct_table<T>(r);
   }
   // ndim == 3
-  if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, Cfg3D<T, Heat3D, xhalo<T, 1>(), 4>>(r);
-  if (shape_matches<Box<1, 7, false>>(c))
-    return run_march_or_direct<T, Cfg3D<T, Box<1, 7, false>, xhalo<T, 1>(), 4>>(r);
-  if (shape_matches<StarPair3D<4>>(c))
-    return run_march_or_direct<T, Cfg3D<T, StarPair3D<4>, xhalo<T, 4>(), 3>>(r);
-  if (shape_matches<WStar7>(c))
-    return run_march2<T, Cfg3D<T, WStar7, xhalo<T, 1>(), 4>, Cfg3D<T, WStar7, 1, 4>>(r);
-  if (shape_matches<Box<2, 7, false>>(c))
-    return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, xhalo<T, 2>(), 3>>(r);
-  if (shape_matches<Box<1, 7, true>>(c))
-    return run_march_or_direct<T, Cfg3D<T, Box<1, 7, true>, xhalo<T, 1>(), 4>>(r);
+  if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, Cfg3D<T, Heat3D, 16, 4, 3>>(r);
+  if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<1, 7, false>, 8, 2, 3>>(r);
+  if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, Cfg3D<T, StarPair3D<4>, 16, 2, 2>>(r);
+  if (shape_matches<WStar7>(c)) return run_march_or_direct<T, Cfg3D<T, WStar7, 16, 4, 3>>(r);
+  if (shape_matches<Box<2, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, 4, 1, 2>>(r);
+  if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<1, 7, true>, 8, 2, 3>>(r);
   return launch_direct_table<T>(r);
 }
 

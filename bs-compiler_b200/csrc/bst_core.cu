@@ -310,9 +310,16 @@ int bst_stencil_apply(const bst_program* prog, int32_t dtype, int32_t ndim, cons
                       const int64_t* x_strides, const void* x, const int64_t* y_strides, void* y,
                       void* stream) {
   clear_error();
-  if (!shape) return fail(BST_ERR_INVALID, "null shape");
-  if (!x || !y) return fail(BST_ERR_INVALID, "null device pointer");
+  if (!shape || !prog) return fail(BST_ERR_INVALID, "null shape or program");
   if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+  if (ndim < 1 || ndim > 3) return fail(BST_ERR_INVALID, "only 1-D, 2-D and 3-D grids are supported");
+  // An empty input or output grid is a no-op (empty tensors may carry null pointers).
+  for (int i = 0; i < ndim; ++i) {
+    if (shape[i] < 0) return fail(BST_ERR_INVALID, "negative extent");
+    if (shape[i] == 0) return BST_OK;
+    if (prog->boundary == BST_BOUNDARY_VALID && prog->out_shape[i] == 0) return BST_OK;
+  }
+  if (!x || !y) return fail(BST_ERR_INVALID, "null device pointer");
   Canon c;
   int rc = canonicalize(prog, ndim, shape, &c);
   if (rc) return rc;

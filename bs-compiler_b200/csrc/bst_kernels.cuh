@@ -16,6 +16,8 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <utility>
+
 #include "bst_shapes.cuh"
 
 namespace bst {
@@ -79,32 +81,105 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 }
 
 // ---------------------------------------------------------------------------------
+// Register-blocked evaluation plan (compile time).
+//
+// Each thread owns VX consecutive x (one 16-byte vector) of PY consecutive rows of the tile
+// and marches along M.  Two sources feed the taps:
+//  * the M-window: when every tap off the current plane is a centre tap (dy = dx = 0, as in
+//    the star stencils), the thread keeps the centre vectors of planes m-WM..m+WM in
+//    registers and loads only the leading plane per step;
+//  * row segments: every other (dm, row) the taps touch is loaded once per step as one
+//    128-bit shared-memory vector per thread, its x-halo taken from neighbouring lanes by
+//    warp shuffles (lanes at a row edge read the halo from shared memory instead).
+struct SegRow {
+  int dm, srow, lo, hi;  // plane offset, row relative to the thread's first row, element range
+};
+template <int N>
+struct SegTable {
+  SegRow r[N > 0 ? N : 1];
+  int n;
+};
+
+template <class S>
+constexpr bool window_mode() {
+  for (int i = 0; i < S::NTAPS; ++i) {
+    const Tap t = S::tbl.taps[i];
+    if (t.dm != 0 && (t.dy != 0 || t.dx != 0)) return false;
+  }
+  return true;
+}
+
+template <class S, int PY, int VX>
+constexpr auto make_segs() {
+  constexpr bool W = window_mode<S>();
+  constexpr int NMAX = (2 * S::RM + 1) * (PY + 2 * S::RY);
+  SegTable<NMAX> t{};
+  t.n = 0;
+  for (int j = 0; j < PY; ++j)
+    for (int i = 0; i < S::NTAPS; ++i) {
+      const Tap tp = S::tbl.taps[i];
+      if (W && (tp.dm != 0 || (tp.dy == 0 && tp.dx == 0))) continue;  // from the window
+      const int srow = j + tp.dy;
+      int k = 0;
+      while (k < t.n && !(t.r[k].dm == tp.dm && t.r[k].srow == srow)) ++k;
+      if (k == t.n) {
+        t.r[k] = SegRow{tp.dm, srow, tp.dx, VX - 1 + tp.dx};
+        ++t.n;
+      } else {
+        t.r[k].lo = t.r[k].lo < tp.dx ? t.r[k].lo : tp.dx;
+        t.r[k].hi = t.r[k].hi > VX - 1 + tp.dx ? t.r[k].hi : VX - 1 + tp.dx;
+      }
+    }
+  return t;
+}
+
+template <class S>
+constexpr int window_depth() {
+  int w = 0;
+  for (int i = 0; i < S::NTAPS; ++i) w = cmax(w, cabs(S::tbl.taps[i].dm));
+  return window_mode<S>() ? w : 0;
+}
+
+// ---------------------------------------------------------------------------------
 // March kernel configuration (compile time).
-template <typename T, class S, int TX_, int TY_, int NTY_, int RB_, int NSX_, int XC_>
+template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_>
 struct MarchCfg {
   using shape = S;
-  static constexpr int TX = TX_;    // output columns per tile (= threads in x)
-  static constexpr int TY = TY_;    // output rows per tile
-  static constexpr int NTY = NTY_;  // thread rows
-  static constexpr int RB = RB_;    // planes per stage (power of two)
+  static constexpr int VX = 16 / int(sizeof(T));   // elements per 16-byte vector
+  static constexpr int TX = TX_;                   // output columns per tile
+  static constexpr int TY = TY_;                   // output rows per tile
+  static constexpr int PY = PY_;                   // rows per thread
+  static constexpr int RB = RB_;                   // planes per stage (power of two)
   static constexpr int RM = S::RM, RY = S::RY, RX = S::RX;
-  static constexpr int V16 = 16 / int(sizeof(T));  // elements per 16 bytes
-  static constexpr int XC = XC_;                   // tile column of output x0
-  static constexpr int TXL = round_up_c(XC + TX + RX, V16);  // loaded columns (<= 256)
-  static constexpr int TYL = TY + 2 * RY;                     // loaded rows
-  static constexpr int PLANE = TXL * TYL;                     // elements per plane tile
+  static constexpr int LPR = TX / VX;              // lanes per tile row
+  static constexpr int NRG = TY / PY;              // row groups
+  static constexpr int THREADS = LPR * NRG;
+  static constexpr int HX = ((RX + VX - 1) / VX) * VX;  // x halo, whole vectors
+  static constexpr int XC = HX;                    // tile column of output x0 (16-byte aligned)
+  static constexpr int TXL = TX + 2 * HX;          // loaded columns (<= 256)
+  static constexpr int TYL = TY + 2 * RY;          // loaded rows
+  static constexpr int PLANE = TXL * TYL;          // elements per plane tile
   static constexpr int STAGE_BYTES = round_up_c(PLANE * RB * int(sizeof(T)), 128);
   static constexpr int STAGE = STAGE_BYTES / int(sizeof(T));
   static constexpr int NEED = 1 + (RB - 1 + 2 * RM) / RB;  // stages one group reads
   static constexpr int NS = NEED + NSX_;                   // ring depth (NSX = prefetch)
-  static constexpr int THREADS = TX * NTY;
-  static constexpr int ROWS = RB * TY;                // (plane,row) pairs per group
-  static constexpr int PER_THREAD = ROWS / NTY;       // points per thread per group
-  static constexpr int SMEM = NS * STAGE_BYTES + 128; // + alignment slack
+  static constexpr int SMEM = NS * STAGE_BYTES + 128;      // + alignment slack
+  static constexpr bool WINDOW = window_mode<S>();
+  static constexpr int WM = window_depth<S>();
+  static constexpr auto SEGS = make_segs<S, PY, VX>();
+  static constexpr int NSEG = SEGS.n;
+  static constexpr int SEGW = VX + 2 * HX;
   static_assert(TXL <= 256 && TYL <= 256 && RB <= 256, "TMA box extent");
-  static_assert(ROWS % NTY == 0, "thread rows must divide the group");
-  static_assert(XC >= RX, "halo column");
+  static_assert(TX % VX == 0 && (LPR & (LPR - 1)) == 0 && LPR <= 32, "lanes per row: power of two <= 32");
+  static_assert(TY % PY == 0 && THREADS % 32 == 0, "whole warps");
   static_assert((RB & (RB - 1)) == 0, "RB power of two");
+  static_assert(RX <= 2 * VX, "x halo within two neighbouring lanes");
+
+  static constexpr int seg_index(int dm, int srow) {
+    for (int k = 0; k < SEGS.n; ++k)
+      if (SEGS.r[k].dm == dm && SEGS.r[k].srow == srow) return k;
+    return -1;
+  }
 };
 
 struct MarchArgs {
@@ -112,29 +187,138 @@ struct MarchArgs {
   int tiles_x, tiles_y, chunk, n_chunks;
   long long n_items;
   unsigned* err;
+  int vec_store;  // output rows are 16-byte aligned and contiguous in x
 };
 
-template <typename T, int RM, int TXL>
-struct RingFetch {
-  const T* pl[2 * RM + 1];
-  int off;
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+  using type = float4;
+  static constexpr int N = 4;
+};
+template <>
+struct Vec16<double> {
+  using type = double2;
+  static constexpr int N = 2;
+};
+
+// Per-thread register state of the march: window and row segments.
+template <typename T, class C>
+struct MarchRegs {
+  T win[2 * C::WM + 1][C::PY][C::VX];
+  T seg[C::NSEG > 0 ? C::NSEG : 1][C::SEGW];
+};
+
+template <typename T, class C, int J, int V>
+struct PointFetch {
+  const MarchRegs<T, C>& r;
   template <int dm, int dy, int dx>
   __device__ __forceinline__ T get() const {
-    return pl[dm + RM][off + dy * TXL + dx];
+    if constexpr (C::WINDOW && (dm != 0 || (dy == 0 && dx == 0))) {
+      return r.win[C::WM + dm][J][V];
+    } else {
+      constexpr int k = C::seg_index(dm, J + dy);
+      static_assert(k >= 0, "tap without a row segment");
+      return r.seg[k][C::HX + V + dx];
+    }
   }
 };
+
+template <typename T, int N>
+__device__ __forceinline__ void lds_vec(const T* p, T (&v)[N]) {
+  using VT = typename Vec16<T>::type;
+  const VT q = *reinterpret_cast<const VT*>(p);
+  const T* e = reinterpret_cast<const T*>(&q);
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = e[i];
+}
+
+// Load row segment K for the plane whose tile starts at `pl` (dm already applied).
+template <typename T, class C, int K>
+__device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, int row0, int lane_x) {
+  constexpr SegRow R = C::SEGS.r[K];
+  const T* rowp = pl + (row0 + R.srow + C::RY) * C::TXL + C::XC + lane_x * C::VX;
+  T own[C::VX];
+  if constexpr (C::WINDOW && R.dm == 0 && R.srow >= 0 && R.srow < C::PY) {
+#pragma unroll
+    for (int e = 0; e < C::VX; ++e) own[e] = r.win[C::WM][R.srow][e];
+  } else {
+    lds_vec<T, C::VX>(rowp, own);
+  }
+#pragma unroll
+  for (int e = 0; e < C::VX; ++e) r.seg[K][C::HX + e] = own[e];
+#pragma unroll
+  for (int e = R.lo; e < 0; ++e) {
+    constexpr int dummy = 0;
+    (void)dummy;
+    const int d = (-e + C::VX - 1) / C::VX;  // lanes to the left holding element e
+    T v = __shfl_up_sync(0xffffffffu, own[e + d * C::VX], d, C::LPR);
+    if (lane_x < d) v = rowp[e];
+    r.seg[K][C::HX + e] = v;
+  }
+#pragma unroll
+  for (int e = C::VX; e <= R.hi; ++e) {
+    const int d = e / C::VX;  // lanes to the right holding element e
+    T v = __shfl_down_sync(0xffffffffu, own[e - d * C::VX], d, C::LPR);
+    if (lane_x >= C::LPR - d) v = rowp[e];
+    r.seg[K][C::HX + e] = v;
+  }
+}
+
+template <typename T, class C, int... Ks>
+__device__ __forceinline__ void load_segments(MarchRegs<T, C>& r, const T* const* pls, int row0, int lane_x,
+                                              std::integer_sequence<int, Ks...>) {
+  (load_segment<T, C, Ks>(r, pls[C::SEGS.r[Ks].dm + C::RM], row0, lane_x), ...);
+}
+
+template <typename T, class C, int J, int... Vs>
+__device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c, T (&res)[C::VX],
+                                         std::integer_sequence<int, Vs...>) {
+  ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs>{r}, c)), ...);
+}
+
+template <typename T, class C, int... Js>
+__device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+                                           T* __restrict__ out, const MarchArgs& a, long long mo, int yrow0,
+                                           int xo, std::integer_sequence<int, Js...>) {
+  (
+      [&] {
+        T res[C::VX];
+        eval_row<T, C, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
+        const int yo = yrow0 + Js;
+        if (yo < a.g.no[1]) {
+          T* dst = out + mo * a.g.so[0] + (long long)yo * a.g.so[1];
+          if (a.vec_store && xo + C::VX <= a.g.no[2]) {
+            using VT = typename Vec16<T>::type;
+            VT q;
+            T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+            for (int v = 0; v < C::VX; ++v) e[v] = res[v];
+            *reinterpret_cast<VT*>(dst + xo) = q;
+          } else {
+#pragma unroll
+            for (int v = 0; v < C::VX; ++v)
+              if (xo + v < a.g.no[2]) dst[(long long)(xo + v) * a.g.so[2]] = res[v];
+          }
+        }
+      }(),
+      ...);
+}
 
 template <typename T, class C>
 __global__ void __launch_bounds__(C::THREADS)
     march_tma_kernel(const __grid_constant__ CUtensorMap tmap, T* __restrict__ out,
                      const MarchArgs a, const Coefs<T, C::shape::NTERMS> coef) {
-  using S = typename C::shape;
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[C::NS];
   T* ring = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
 
-  const int tx = threadIdx.x, ty = threadIdx.y;
-  const bool leader = (tx == 0 && ty == 0);
+  const int t = threadIdx.x;
+  const int lane_x = t % C::LPR;
+  const int rg = t / C::LPR;
+  const int row0 = rg * C::PY;  // first tile row of this thread
+  const bool leader = (t == 0);
   if (leader) {
     for (int i = 0; i < C::NS; ++i) mbar_init(&bars[i], 1);
     mbar_fence_init();
@@ -146,6 +330,7 @@ __global__ void __launch_bounds__(C::THREADS)
   int n_issued = 0;        // stages of the current item issued so far
   int n_waited = 0;        // stages of the current item waited on so far
   bool failed = false;
+  MarchRegs<T, C> r;
 
   for (long long item = blockIdx.x; item < a.n_items; item += gridDim.x) {
     const int tile_x = int(item % a.tiles_x);
@@ -167,6 +352,11 @@ __global__ void __launch_bounds__(C::THREADS)
       const unsigned slot = (q_base + unsigned(q)) % C::NS;
       mbar_expect_tx(&bars[slot], unsigned(C::PLANE * C::RB * sizeof(T)));
       tma_load_3d(ring + size_t(slot) * C::STAGE, &tmap, &bars[slot], cx, cy, L0 + q * C::RB);
+    };
+    // Shared-memory tile of input plane `rel` (relative to L0).
+    auto plane = [&](int rel) -> const T* {
+      const unsigned slot = (q_base + unsigned(rel / C::RB)) % C::NS;
+      return ring + size_t(slot) * C::STAGE + size_t(rel % C::RB) * C::PLANE;
     };
     __syncthreads();  // the previous item's last group is done with the ring
     n_issued = qt < C::NS ? qt : C::NS;
@@ -195,26 +385,43 @@ __global__ void __launch_bounds__(C::THREADS)
         }
         ++n_issued;
       }
-
-      const long long m_grp = mb + (long long)grp * C::RB;
+      if constexpr (C::WINDOW) {
+        if (grp == 0) {  // fill the window with planes mb-WM .. mb+WM-1
 #pragma unroll
-      for (int k = 0; k < C::PER_THREAD; ++k) {
-        const int w = ty + k * C::NTY;
-        const int p = w / C::TY;
-        const int yl = w % C::TY;
-        const long long mo = m_grp + p;
-        const int yo = y0 + yl, xo = x0 + tx;
-        RingFetch<T, C::RM, C::TXL> f;
+          for (int k = 0; k < 2 * C::WM; ++k) {
+            const T* pl = plane(C::RM - C::WM + k);
 #pragma unroll
-        for (int d = 0; d < 2 * C::RM + 1; ++d) {
-          const int rel = grp * C::RB + p + d;  // input plane relative to L0
-          const unsigned slot = (q_base + unsigned(rel / C::RB)) % C::NS;
-          f.pl[d] = ring + size_t(slot) * C::STAGE + size_t(rel % C::RB) * C::PLANE;
+            for (int j = 0; j < C::PY; ++j)
+              lds_vec<T, C::VX>(pl + (row0 + j + C::RY) * C::TXL + C::XC + lane_x * C::VX, r.win[k][j]);
+          }
         }
-        f.off = (yl + C::RY) * C::TXL + C::XC + tx;
-        const T v = eval_shape<S, T>(f, coef);
-        if (mo < me && yo < g.no[1] && xo < g.no[2])
-          out[mo * g.so[0] + (long long)yo * g.so[1] + (long long)xo * g.so[2]] = v;
+      }
+      for (int p = 0; p < C::RB; ++p) {
+        const long long mo = mb + (long long)grp * C::RB + p;
+        if (mo >= me) break;
+        const int rel0 = int(mo - mb) + C::RM;  // plane of dm = 0
+        if constexpr (C::WINDOW) {
+          const T* pl = plane(rel0 + C::WM);
+#pragma unroll
+          for (int j = 0; j < C::PY; ++j)
+            lds_vec<T, C::VX>(pl + (row0 + j + C::RY) * C::TXL + C::XC + lane_x * C::VX, r.win[2 * C::WM][j]);
+        }
+        if constexpr (C::NSEG > 0) {
+          const T* pls[2 * C::RM + 1];
+#pragma unroll
+          for (int d = 0; d < 2 * C::RM + 1; ++d) pls[d] = plane(rel0 + d - C::RM);
+          load_segments<T, C>(r, pls, row0, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+        }
+        eval_store<T, C>(r, coef, out, a, mo, y0 + row0, x0 + lane_x * C::VX,
+                         std::make_integer_sequence<int, C::PY>{});
+        if constexpr (C::WINDOW) {
+#pragma unroll
+          for (int k = 0; k < 2 * C::WM; ++k)
+#pragma unroll
+            for (int j = 0; j < C::PY; ++j)
+#pragma unroll
+              for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
+        }
       }
     }
     if (failed) break;
@@ -292,23 +499,6 @@ __global__ void __launch_bounds__(256)
 // ---------------------------------------------------------------------------------
 // 1-D line kernel.  Each thread owns V = 16/sizeof(T) consecutive outputs; its input
 // window is gathered from its own 16-byte vector and its neighbours' through shuffles.
-template <typename T>
-struct Vec16;
-template <>
-struct Vec16<float> {
-  using type = float4;
-  static constexpr int N = 4;
-};
-template <>
-struct Vec16<double> {
-  using type = double2;
-  static constexpr int N = 2;
-};
-
-template <typename T, int N>
-struct VecRegs {
-  T v[N];
-};
 
 template <typename T>
 __device__ __forceinline__ void load_vec(const T* p, T* dst) {

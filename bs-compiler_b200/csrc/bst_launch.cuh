@@ -144,8 +144,8 @@ bool march_eligible(const LaunchReq& r) {
   if (r.xs[0] <= 0 || r.xs[1] <= 0) return false;
   for (int i = 0; i < 3; ++i)
     if (c.n[i] >= (int64_t(1) << 31) || c.no[i] >= (int64_t(1) << 31)) return false;
-  // The tile's first loaded column must sit on a 16-byte boundary.
-  if (((c.org[2] - C::XC) % C::V16 + C::V16) % C::V16 != 0) return false;
+  // The tile's first loaded column and every thread's vector sit on 16-byte boundaries.
+  if (((c.org[2] - C::XC) % C::VX + C::VX) % C::VX != 0) return false;
   if (c.R[0] > C::RM || c.R[1] > C::RY || c.R[2] > C::RX) return false;
   return true;
 }
@@ -220,8 +220,12 @@ int launch_march(const LaunchReq& r) {
   a.n_items = (long long)a.tiles_x * a.tiles_y * nchunks;
   a.err = device_error_word();
   if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
+  a.vec_store = (reinterpret_cast<uintptr_t>(r.y) % 16 == 0 && r.ys[2] == 1 && (r.ys[1] * E) % 16 == 0 &&
+                 (r.ys[0] * E) % 16 == 0)
+                    ? 1
+                    : 0;
   const long long grid = a.n_items < resident ? a.n_items : resident;
-  dim3 block(C::TX, C::NTY);
+  dim3 block(C::THREADS);
   kern<<<unsigned(grid), block, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
                                                   make_coefs<T, C::shape::NTERMS>(c));
   BST_CUDA(cudaGetLastError());
