@@ -235,10 +235,11 @@ __device__ __forceinline__ void lds_vec(const T* p, T (&v)[N]) {
 }
 
 // Load row segment K for the plane whose tile starts at `pl` (dm already applied).
+// `pl` points at the thread's first vector (row 0 of its rows) in the plane tile.
 template <typename T, class C, int K>
-__device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, int row0, int lane_x) {
+__device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, int /*unused*/, int lane_x) {
   constexpr SegRow R = C::SEGS.r[K];
-  const T* rowp = pl + (row0 + R.srow + C::RY) * C::TXL + C::XC + lane_x * C::VX;
+  const T* rowp = pl + R.srow * C::TXL;
   T own[C::VX];
   if constexpr (C::WINDOW && R.dm == 0 && R.srow >= 0 && R.srow < C::PY) {
 #pragma unroll
@@ -266,44 +267,85 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
   }
 }
 
-template <typename T, class C, int... Ks>
-__device__ __forceinline__ void load_segments(MarchRegs<T, C>& r, const T* const* pls, int row0, int lane_x,
-                                              std::integer_sequence<int, Ks...>) {
-  (load_segment<T, C, Ks>(r, pls[C::SEGS.r[Ks].dm + C::RM], row0, lane_x), ...);
-}
-
 template <typename T, class C, int J, int... Vs>
 __device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c, T (&res)[C::VX],
                                          std::integer_sequence<int, Vs...>) {
   ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs>{r}, c)), ...);
 }
 
+// Evaluate the PY x VX points of one plane step and store them.  `dst` points at the
+// thread's first output of row 0 of this plane; `interior` = the whole tile is inside the
+// output and rows are 16-byte aligned (unchecked vector stores).
 template <typename T, class C, int... Js>
 __device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
-                                           T* __restrict__ out, const MarchArgs& a, long long mo, int yrow0,
-                                           int xo, std::integer_sequence<int, Js...>) {
+                                           T* __restrict__ dst, long long so1, bool interior, int rows_left,
+                                           int cols_left, long long so2, std::integer_sequence<int, Js...>) {
+  using VT = typename Vec16<T>::type;
   (
       [&] {
         T res[C::VX];
         eval_row<T, C, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
-        const int yo = yrow0 + Js;
-        if (yo < a.g.no[1]) {
-          T* dst = out + mo * a.g.so[0] + (long long)yo * a.g.so[1];
-          if (a.vec_store && xo + C::VX <= a.g.no[2]) {
-            using VT = typename Vec16<T>::type;
-            VT q;
-            T* e = reinterpret_cast<T*>(&q);
+        T* d = dst + Js * so1;
+        if (interior) {
+          VT q;
+          T* e = reinterpret_cast<T*>(&q);
 #pragma unroll
-            for (int v = 0; v < C::VX; ++v) e[v] = res[v];
-            *reinterpret_cast<VT*>(dst + xo) = q;
-          } else {
+          for (int v = 0; v < C::VX; ++v) e[v] = res[v];
+          *reinterpret_cast<VT*>(d) = q;
+        } else if (Js < rows_left) {
 #pragma unroll
-            for (int v = 0; v < C::VX; ++v)
-              if (xo + v < a.g.no[2]) dst[(long long)(xo + v) * a.g.so[2]] = res[v];
-          }
+          for (int v = 0; v < C::VX; ++v)
+            if (v < cols_left) d[v * so2] = res[v];
         }
       }(),
       ...);
+}
+
+// Shared-memory tile of the input plane at offset REL from the group's first input plane.
+template <typename T, class C, int REL>
+__device__ __forceinline__ const T* stage_plane(const T* const* sb) {
+  return sb[REL / C::RB] + (REL % C::RB) * C::PLANE;
+}
+
+template <typename T, class C, int P, int... Ks>
+__device__ __forceinline__ void load_segments_at(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                                 std::integer_sequence<int, Ks...>) {
+  (load_segment<T, C, Ks>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
+}
+
+// One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store, rotate.
+template <typename T, class C, int P>
+__device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                           const Coefs<T, C::shape::NTERMS>& coef, T* dst, long long so1,
+                                           bool interior, int rows_left, int cols_left, long long so2) {
+  if constexpr (C::WINDOW) {
+    const T* pl = stage_plane<T, C, P + C::RM + C::WM>(sb) + toff;
+#pragma unroll
+    for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[2 * C::WM][j]);
+  }
+  if constexpr (C::NSEG > 0)
+    load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+  eval_store<T, C>(r, coef, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
+  if constexpr (C::WINDOW) {
+#pragma unroll
+    for (int k = 0; k < 2 * C::WM; ++k)
+#pragma unroll
+      for (int j = 0; j < C::PY; ++j)
+#pragma unroll
+        for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
+  }
+}
+
+template <typename T, class C, int... Ps>
+__device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                            const Coefs<T, C::shape::NTERMS>& coef, T* dst0, long long so0,
+                                            long long so1, bool interior, int rows_left, int cols_left,
+                                            long long so2, int planes, std::integer_sequence<int, Ps...>) {
+  // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
+  ((Ps < planes ? plane_step<T, C, Ps>(r, sb, toff, lane_x, coef, dst0 + Ps * so0, so1, interior, rows_left,
+                                       cols_left, so2)
+                : void()),
+   ...);
 }
 
 template <typename T, class C>
@@ -319,6 +361,8 @@ __global__ void __launch_bounds__(C::THREADS)
   const int rg = t / C::LPR;
   const int row0 = rg * C::PY;  // first tile row of this thread
   const bool leader = (t == 0);
+  // Offset of the thread's first vector inside a plane tile.
+  const int toff = (row0 + C::RY) * C::TXL + C::XC + lane_x * C::VX;
   if (leader) {
     for (int i = 0; i < C::NS; ++i) mbar_init(&bars[i], 1);
     mbar_fence_init();
@@ -347,16 +391,17 @@ __global__ void __launch_bounds__(C::THREADS)
     const int cx = x0 + g.org[2] - C::XC;
     const int cy = y0 + g.org[1] - C::RY;
     const int L0 = int(mb + g.org[0] - C::RM);
+    // Output addressing of this thread for the item.
+    const int xo = x0 + lane_x * C::VX, yo = y0 + row0;
+    const int rows_left = int(g.no[1] - yo);
+    const int cols_left = int(g.no[2] - xo);
+    const bool interior = a.vec_store && x0 + C::TX <= g.no[2] && y0 + C::TY <= g.no[1];
+    T* out_item = out + mb * g.so[0] + (long long)yo * g.so[1] + (long long)xo * g.so[2];
 
     auto issue = [&](int q) {
       const unsigned slot = (q_base + unsigned(q)) % C::NS;
       mbar_expect_tx(&bars[slot], unsigned(C::PLANE * C::RB * sizeof(T)));
       tma_load_3d(ring + size_t(slot) * C::STAGE, &tmap, &bars[slot], cx, cy, L0 + q * C::RB);
-    };
-    // Shared-memory tile of input plane `rel` (relative to L0).
-    auto plane = [&](int rel) -> const T* {
-      const unsigned slot = (q_base + unsigned(rel / C::RB)) % C::NS;
-      return ring + size_t(slot) * C::STAGE + size_t(rel % C::RB) * C::PLANE;
     };
     __syncthreads();  // the previous item's last group is done with the ring
     n_issued = qt < C::NS ? qt : C::NS;
@@ -385,44 +430,31 @@ __global__ void __launch_bounds__(C::THREADS)
         }
         ++n_issued;
       }
+      // Stage tiles read by this group.
+      const T* sb[C::NEED];
+      {
+        unsigned slot = (q_base + unsigned(grp)) % C::NS;
+#pragma unroll
+        for (int k = 0; k < C::NEED; ++k) {
+          sb[k] = ring + size_t(slot) * C::STAGE;
+          slot = slot + 1 == unsigned(C::NS) ? 0u : slot + 1;
+        }
+      }
       if constexpr (C::WINDOW) {
         if (grp == 0) {  // fill the window with planes mb-WM .. mb+WM-1
 #pragma unroll
           for (int k = 0; k < 2 * C::WM; ++k) {
-            const T* pl = plane(C::RM - C::WM + k);
+            const int rel = C::RM - C::WM + k;
+            const T* pl = sb[rel / C::RB] + (rel % C::RB) * C::PLANE + toff;
 #pragma unroll
-            for (int j = 0; j < C::PY; ++j)
-              lds_vec<T, C::VX>(pl + (row0 + j + C::RY) * C::TXL + C::XC + lane_x * C::VX, r.win[k][j]);
+            for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[k][j]);
           }
         }
       }
-      for (int p = 0; p < C::RB; ++p) {
-        const long long mo = mb + (long long)grp * C::RB + p;
-        if (mo >= me) break;
-        const int rel0 = int(mo - mb) + C::RM;  // plane of dm = 0
-        if constexpr (C::WINDOW) {
-          const T* pl = plane(rel0 + C::WM);
-#pragma unroll
-          for (int j = 0; j < C::PY; ++j)
-            lds_vec<T, C::VX>(pl + (row0 + j + C::RY) * C::TXL + C::XC + lane_x * C::VX, r.win[2 * C::WM][j]);
-        }
-        if constexpr (C::NSEG > 0) {
-          const T* pls[2 * C::RM + 1];
-#pragma unroll
-          for (int d = 0; d < 2 * C::RM + 1; ++d) pls[d] = plane(rel0 + d - C::RM);
-          load_segments<T, C>(r, pls, row0, lane_x, std::make_integer_sequence<int, C::NSEG>{});
-        }
-        eval_store<T, C>(r, coef, out, a, mo, y0 + row0, x0 + lane_x * C::VX,
-                         std::make_integer_sequence<int, C::PY>{});
-        if constexpr (C::WINDOW) {
-#pragma unroll
-          for (int k = 0; k < 2 * C::WM; ++k)
-#pragma unroll
-            for (int j = 0; j < C::PY; ++j)
-#pragma unroll
-              for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
-        }
-      }
+      const long long m_grp = (long long)grp * C::RB;
+      const int planes = int(me - mb - m_grp);
+      group_steps<T, C>(r, sb, toff, lane_x, coef, out_item + m_grp * g.so[0], g.so[0], g.so[1], interior,
+                        rows_left, cols_left, g.so[2], planes, std::make_integer_sequence<int, C::RB>{});
     }
     if (failed) break;
     q_base += unsigned(qt);
