@@ -210,10 +210,17 @@ def run_basalto(args):
 
     if ws == 1:
         a = w.make_input(device=dev)
-        b = torch.empty_like(a)
+        if prog.boundary == "zero":
+            b = torch.empty_like(a)
 
-        def step():
-            basalto.sweeps(prog, a, b, sweeps)
+            def step():
+                basalto.sweeps(prog, a, b, sweeps)
+        else:  # a shrinking (valid-region) stencil: one sweep per step into its own output
+            b = torch.empty(prog.out_shape(a.shape), dtype=a.dtype, device=dev)
+
+            def step():
+                for _ in range(sweeps):
+                    basalto.apply(prog, a, out=b)
 
         points_job = w.points
         launches_per_step = sweeps

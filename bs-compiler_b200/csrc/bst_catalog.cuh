@@ -58,13 +58,53 @@ int run_line(const LaunchReq& r) {
 
 // Tile configurations.  A tile row is one warp of 16-byte vectors: 128 fp32 or 64 fp64
 // columns.  2-D grids march along rows with one-warp CTAs (many resident per SM);
-// 3-D tiles stack PY-row groups of warps and march along Z.
+// 3-D tiles stack PY-row groups of warps and march along Z.  The defaults below were chosen
+// by measurement on B200 (rows per tile, rows per thread, prefetch stages).
+#ifndef BST_2D_RB
+#define BST_2D_RB 4
+#endif
+#ifndef BST_2D_NSX
+#define BST_2D_NSX 2
+#endif
+#ifndef BST_HEAT_TY
+#define BST_HEAT_TY 16
+#endif
+#ifndef BST_HEAT_PY
+#define BST_HEAT_PY 4
+#endif
+#ifndef BST_HEAT_NSX
+#define BST_HEAT_NSX 3
+#endif
+#ifndef BST_BOX_TY
+#define BST_BOX_TY 8
+#endif
+#ifndef BST_BOX_PY
+#define BST_BOX_PY 2
+#endif
+#ifndef BST_BOX_NSX
+#define BST_BOX_NSX 3
+#endif
+#ifndef BST_STAR_TY
+#define BST_STAR_TY 16
+#endif
+#ifndef BST_STAR_PY
+#define BST_STAR_PY 2
+#endif
+#ifndef BST_STAR_NSX
+#define BST_STAR_NSX 4
+#endif
 template <typename T>
 constexpr int kRowCols = 32 * (16 / int(sizeof(T)));
 template <typename T, class S>
-using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, 4, 2>;
+using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, BST_2D_RB, BST_2D_NSX>;
 template <typename T, class S, int TY, int PY, int NSX>
 using Cfg3D = MarchCfg<T, S, kRowCols<T>, TY, PY, 1, NSX>;
+template <typename T, class S>
+using CfgHeat = Cfg3D<T, S, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_NSX>;
+template <typename T, class S>
+using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX>;
+template <typename T, class S>
+using CfgStar = Cfg3D<T, S, BST_STAR_TY, BST_STAR_PY, BST_STAR_NSX>;
 
 template <typename T>
 int dispatch_sweep(const LaunchReq& r) {
@@ -88,12 +128,12 @@ int dispatch_sweep(const LaunchReq& r) {
     return launch_direct_table<T>(r);
   }
   // ndim == 3
-  if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, Cfg3D<T, Heat3D, 16, 4, 3>>(r);
-  if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<1, 7, false>, 8, 2, 3>>(r);
-  if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, Cfg3D<T, StarPair3D<4>, 16, 2, 2>>(r);
-  if (shape_matches<WStar7>(c)) return run_march_or_direct<T, Cfg3D<T, WStar7, 16, 4, 3>>(r);
+  if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, CfgHeat<T, Heat3D>>(r);
+  if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, false>>>(r);
+  if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, CfgStar<T, StarPair3D<4>>>(r);
+  if (shape_matches<WStar7>(c)) return run_march_or_direct<T, CfgHeat<T, WStar7>>(r);
   if (shape_matches<Box<2, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, 4, 1, 2>>(r);
-  if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<1, 7, true>, 8, 2, 3>>(r);
+  if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, true>>>(r);
   return launch_direct_table<T>(r);
 }
 

@@ -161,11 +161,16 @@ struct MarchCfg {
   static constexpr int PLANE = TXL * TYL;          // elements per plane tile
   static constexpr int STAGE_BYTES = round_up_c(PLANE * RB * int(sizeof(T)), 128);
   static constexpr int STAGE = STAGE_BYTES / int(sizeof(T));
-  static constexpr int NEED = 1 + (RB - 1 + 2 * RM) / RB;  // stages one group reads
-  static constexpr int NS = NEED + NSX_;                   // ring depth (NSX = prefetch)
-  static constexpr int SMEM = NS * STAGE_BYTES + 128;      // + alignment slack
   static constexpr bool WINDOW = window_mode<S>();
   static constexpr int WM = window_depth<S>();
+  // Stages read by group g (input planes g*RB + [0, RB-1+2RM] relative to the item's first
+  // loaded plane): the window keeps planes behind the current one in registers, so in window
+  // mode group g only reads from plane g*RB + RM on and earlier stages retire early.
+  static constexpr int NEED = 1 + (RB - 1 + 2 * RM) / RB;  // stages of group 0 (incl. window fill)
+  static constexpr int FIRST_OFF = (WINDOW ? RM : 0) / RB;  // first stage still read, minus g
+  static constexpr int SPAN = NEED - FIRST_OFF;            // stages one steady-state group reads
+  static constexpr int NS = NEED > SPAN + NSX_ ? NEED : SPAN + NSX_;  // ring depth
+  static constexpr int SMEM = NS * STAGE_BYTES + 128;      // + alignment slack
   static constexpr auto SEGS = make_segs<S, PY, VX>();
   static constexpr int NSEG = SEGS.n;
   static constexpr int SEGW = VX + 2 * HX;
@@ -423,12 +428,17 @@ __global__ void __launch_bounds__(C::THREADS)
         failed = true;
         break;
       }
-      if (grp >= 1 && grp - 1 + C::NS < qt) {
-        if (leader) {
-          fence_proxy_async_smem();
-          issue(grp - 1 + C::NS);
+      if (grp >= 1) {
+        // Stages before FIRST(grp) are retired: refill the ring up to FIRST(grp) + NS.
+        const int lim = grp + C::FIRST_OFF + C::NS;
+        const int target = qt < lim ? qt : lim;
+        if (n_issued < target) {
+          if (leader) {
+            fence_proxy_async_smem();
+            for (int q = n_issued; q < target; ++q) issue(q);
+          }
+          n_issued = target;
         }
-        ++n_issued;
       }
       // Stage tiles read by this group.
       const T* sb[C::NEED];

@@ -29,6 +29,7 @@ CUDA_HOME = Path(NVCC).resolve().parent.parent
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "--expt-relaxed-constexpr",
                   "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}"]
+NVFLAGS += os.environ.get("BST_NVCC_EXTRA", "").split()  # e.g. tile-size macros for tuning builds
 
 KERNEL_UNITS = ["bst_core.cu", "bst_f32.cu", "bst_f64.cu", "bst_interceptor.cu", "bst_halo.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [INCLUDE / "basalto_b200.h"]
