@@ -300,7 +300,7 @@ def run_basalto(args):
     e2e = None
     if ws == 1 and args.e2e_steps > 0:
         host_in = w.make_input().pin_memory() if args.host_input else torch.empty(w.shape, dtype=w.dtype).pin_memory()
-        host_out = torch.empty(w.shape, dtype=w.dtype).pin_memory()
+        host_out = torch.empty(prog.out_shape(w.shape), dtype=w.dtype).pin_memory()
         torch._dynamo.reset()
         cf = torch.compile(w.fn, backend="basalto")
 
@@ -319,9 +319,8 @@ def run_basalto(args):
         f1.record(stream)
         torch.cuda.synchronize()
         e_ms = f0.elapsed_time(f1) / args.e2e_steps
-        nbytes = w.points * es
         e2e = {"value": round(w.points * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
-               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes, "ms_per_step": round(e_ms, 3),
+               "h2d_bytes_per_step": w.points * es, "d2h_bytes_per_step": w.out_points * es, "ms_per_step": round(e_ms, 3),
                "path": "torch.compile(backend='basalto'), one call per sweep, pinned host buffers"}
 
     # ---- CPU baseline (rank 0, N = 1 only, bounded sample) ------------------------------------

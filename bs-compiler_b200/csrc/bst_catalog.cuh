@@ -64,7 +64,7 @@ int run_line(const LaunchReq& r) {
 #define BST_2D_RB 4
 #endif
 #ifndef BST_2D_NSX
-#define BST_2D_NSX 2
+#define BST_2D_NSX 4
 #endif
 #ifndef BST_HEAT_TY
 #define BST_HEAT_TY 16

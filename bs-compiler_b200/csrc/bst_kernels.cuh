@@ -169,7 +169,10 @@ struct MarchCfg {
   static constexpr int NEED = 1 + (RB - 1 + 2 * RM) / RB;  // stages of group 0 (incl. window fill)
   static constexpr int FIRST_OFF = (WINDOW ? RM : 0) / RB;  // first stage still read, minus g
   static constexpr int SPAN = NEED - FIRST_OFF;            // stages one steady-state group reads
-  static constexpr int NS = NEED > SPAN + NSX_ ? NEED : SPAN + NSX_;  // ring depth
+  // Ring depth.  A group waits before its barrier and refills after it, so every stage a
+  // group waits for must have been issued one group earlier: NS >= NEED + 1 covers group 1
+  // (from the initial fill) and every later group (from the previous group's refill).
+  static constexpr int NS = NEED + 1 > SPAN + NSX_ ? NEED + 1 : SPAN + NSX_;
   static constexpr int SMEM = NS * STAGE_BYTES + 128;      // + alignment slack
   static constexpr auto SEGS = make_segs<S, PY, VX>();
   static constexpr int NSEG = SEGS.n;
@@ -179,6 +182,7 @@ struct MarchCfg {
   static_assert(TY % PY == 0 && THREADS % 32 == 0, "whole warps");
   static_assert((RB & (RB - 1)) == 0, "RB power of two");
   static_assert(RX <= 2 * VX, "x halo within two neighbouring lanes");
+  static_assert(NS >= NEED + 1, "every stage is issued before a group waits on it");
 
   static constexpr int seg_index(int dm, int srow) {
     for (int k = 0; k < SEGS.n; ++k)

@@ -128,6 +128,29 @@ def eval_program(x: np.ndarray, terms, init_zero=False, boundary="zero", shrink=
     return acc
 
 
+def fold_values(tap_values, terms, init_zero=False, dtype=np.float32) -> np.ndarray:
+    """The program's fold over already gathered tap values: tap_values[k] holds the values of
+    the program's k-th tap (terms' taps in order) at a set of output points."""
+    t = np.dtype(dtype).type
+    k = 0
+    acc = None
+    for g, (op, scale, taps) in enumerate(terms):
+        s = np.array(tap_values[k], dtype=dtype, copy=True)
+        k += 1
+        for _ in taps[1:]:
+            s = s + tap_values[k]
+            k += 1
+        if op == "mul":
+            s = t(scale) * s
+        elif op == "div":
+            s = s / t(scale)
+        if g == 0:
+            acc = (np.zeros(s.shape, dtype) + s) if init_zero else s
+        else:
+            acc = acc + s
+    return acc
+
+
 def eval_program_at(x: np.ndarray, points: np.ndarray, terms, init_zero=False, boundary="zero", shrink=()) -> np.ndarray:
     """Program value at output indices `points` (shape [k, ndim]) — for full-size grids,
     where only a sample of outputs can be re-computed on the host."""

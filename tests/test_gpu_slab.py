@@ -1,0 +1,107 @@
+"""Z-slab sweeps on GPUs: bst_slab_sweeps / bst_halo_exchange.
+
+* one rank (an NCCL communicator of size 1): the boundary/interior split and the slab
+  addressing must give exactly the single-grid result;
+* two ranks on two GPUs (skipped with fewer): ghost exchange over NCCL, gathered result equal
+  to the single-grid oracle.  NVLS is off; ranks exchange the NCCL id over gloo; every wait
+  is bounded by process-group and join timeouts.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import stencil_oracle as O
+from conftest import oracle_terms
+
+pytestmark = pytest.mark.gpu
+
+
+def _programs():
+    from basalto import program as P
+    from basalto import workloads as W
+    return [(P.heat7_3d(), (37, 20, 64), torch.float32, 4),
+            (P.jacobi5_2d(), (70, 256), torch.float32, 5),
+            (P.box(3, 1, W.box27_weights()), (19, 16, 64), torch.float64, 3),
+            (P.star_3d(P.LAPLACIAN8_COEFFS), (21, 24, 128), torch.float32, 2)]
+
+
+@pytest.mark.parametrize("idx", range(4))
+def test_single_rank_slab_equals_single_grid(idx):
+    from basalto.slab import SlabDomain
+    import basalto
+    prog, shape, dtype, steps = _programs()[idx]
+    x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(31))
+    dom = SlabDomain(prog, shape, dtype=dtype, device="cuda:0")
+    try:
+        dom.load(x)
+        dom.run(steps)
+        got = dom.owned().cpu().numpy()
+    finally:
+        dom.close()
+    a = x.cuda()
+    b = torch.empty_like(a)
+    ref_gpu = basalto.sweeps(prog, a, b, steps).cpu().numpy()
+    ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
+    assert np.array_equal(got, ref_gpu)
+    assert np.array_equal(got, ref)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from basalto.slab import SlabDomain
+        res = []
+        for prog, shape, dtype, steps in _programs():
+            x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(41))
+            dom = SlabDomain(prog, shape, dtype=dtype, device=f"cuda:{rank}", timeout_s=60.0)
+            try:
+                dom.load(x)
+                dom.run(steps)
+                torch.cuda.synchronize()
+                part = dom.owned().cpu().numpy()
+            finally:
+                dom.close()
+            parts = [None] * world
+            dist.all_gather_object(parts, part)
+            if rank == 0:
+                got = np.concatenate(parts, 0)
+                ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
+                res.append(bool(np.array_equal(got, ref)))
+        if rank == 0:
+            q.put(res)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks_nccl_exchange_equals_single_grid():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = q.get(timeout=300)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert res == [True] * len(_programs())
+    assert all(p.exitcode == 0 for p in procs)
