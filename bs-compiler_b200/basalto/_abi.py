@@ -66,6 +66,9 @@ SIGNATURES = [
     ("bst_stencil_apply", c_int32,
      [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), POINTER(c_int64), c_void_p, POINTER(c_int64),
       c_void_p, c_void_p]),
+    ("bst_stencil_apply_noalloc", c_int32,
+     [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), POINTER(c_int64), c_void_p, POINTER(c_int64),
+      c_void_p, c_void_p]),
     ("bst_stencil_sweeps", c_int32,
      [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_void_p, c_void_p, c_int32, c_void_p]),
     ("bst_device_caps_query", c_int32, [c_int32, POINTER(CDeviceCaps)]),

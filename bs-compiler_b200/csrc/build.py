@@ -31,7 +31,7 @@ NVFLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "--expt-relax
                   "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}"]
 NVFLAGS += os.environ.get("BST_NVCC_EXTRA", "").split()  # e.g. tile-size macros for tuning builds
 
-KERNEL_UNITS = ["bst_core.cu", "bst_f32.cu", "bst_f64.cu", "bst_interceptor.cu", "bst_halo.cu"]
+KERNEL_UNITS = ["bst_core.cu", "bst_f32.cu", "bst_f64.cu", "bst_interceptor.cu", "bst_halo.cu", "bst_noalloc.cu"]
 HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [INCLUDE / "basalto_b200.h"]
 
 LIB = PKG / "libbasalto_b200.so"

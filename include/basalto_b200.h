@@ -118,6 +118,21 @@ BST_API int bst_stencil_apply(const bst_program* prog, int32_t dtype, int32_t nd
                       const int64_t* x_strides, const void* x, const int64_t* y_strides, void* y,
                       void* stream);
 
+/* One sweep y = S(x), same arguments and result as bst_stencil_apply, for callers that
+ * cannot allocate GPU memory during the call (a fixed-budget real-time loop, a host
+ * framework that owns every device byte through its own pool, code that must not hit
+ * cudaMalloc's implicit synchronisation).  No counterpart in the reference.
+ * It always runs the runtime-table kernel, with the program table in a fixed 32 KiB device
+ * array compiled into the library instead of a per-call device buffer: it makes no
+ * cudaMalloc/cudaFree or other allocating call.  Programs whose packed table (16 + 6*ntaps
+ * + 5*nterms + elem*nterms bytes, aligned) exceeds 32 KiB return BST_ERR_UNSUPPORTED.
+ * The array is shared by every call on the device: calls whose work overlaps on the GPU
+ * (different streams, unordered) race; each call rewrites all the table it uses.  The first
+ * call on a device looks up the array's device address; make it before any stream capture. */
+BST_API int bst_stencil_apply_noalloc(const bst_program* prog, int32_t dtype, int32_t ndim,
+                                      const int64_t* shape, const int64_t* x_strides, const void* x,
+                                      const int64_t* y_strides, void* y, void* stream);
+
 /* nsteps sweeps ping-ponging between two C-contiguous same-shape buffers (ZERO boundary
  * programs only): step 1 reads a and writes b, step 2 reads b and writes a, ...; the
  * result is in b when nsteps is odd, in a when even.  The reference runs one sweep per
