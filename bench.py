@@ -161,10 +161,21 @@ class CpuReference:
         return self.w.points * sweeps / dt / 1e9, dt
 
 
+def _workload(args):
+    """The named workload, optionally on a different grid (--shape, e.g. for profiling)."""
+    import dataclasses
+
+    from basalto.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]
+    if args.shape:
+        w = dataclasses.replace(w, shape=tuple(int(v) for v in args.shape.split("x")))
+    return w
+
+
 def run_reference(args):
     ws, rank, local = _dist()
     from basalto.workloads import WORKLOADS
-    w = WORKLOADS[args.workload]
+    w = _workload(args)
     if rank != 0:
         return
     threads = os.cpu_count() or 1
@@ -202,7 +213,7 @@ def run_basalto(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = _init_pg(ws, rank, local, "nccl") if ws > 1 else None
-    w = WORKLOADS[args.workload]
+    w = _workload(args)
     prog = w.program
     sweeps = w.steps
     stream = torch.cuda.current_stream(dev)
@@ -366,6 +377,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="basalto", choices=["basalto", "reference"])
     ap.add_argument("--workload", default="jacobi5_2d")
+    ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
     ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
