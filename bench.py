@@ -234,7 +234,6 @@ def run_basalto(args):
                     basalto.apply(prog, a, out=b)
 
         points_job = w.points
-        launches_per_step = sweeps
         comm = None
     else:
         # Weak scaling: each rank owns a full-size slab; ghost planes along axis 0.
@@ -269,7 +268,6 @@ def run_basalto(args):
                                                   sweeps, sp))
 
         points_job = w.points * ws
-        launches_per_step = sweeps * (3 if local_shape[0] > 2 * R else 2)
 
     # ---- timed region (device time, CUDA events on the compute stream) -------------------
     for _ in range(args.warmup):
@@ -302,37 +300,61 @@ def run_basalto(args):
     value = points_job * sweeps * args.steps / (ms_total * 1e-3) / 1e9
 
     # Dominant kernel: the sweep itself; average launch = timed region / sweeps (per rank).
-    launch_ms = ms_total / (args.steps * sweeps)
+    # Multi-sweep runs fuse several sweeps per launch (temporal blocking); each launch still
+    # reads its input grid once and writes its output once, so the algorithmic traffic of a
+    # launch is 2 * elem bytes per point whatever the number of sweeps it fuses.
+    launch_ms = ms_total / max(1, launches)  # this rank's launches over the timed region
     per_launch_bytes = 2 * es * w.points
     achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
     peak, peak_src = _peaks()
 
-    # ---- e2e through the plugin path with host buffers ------------------------------------
+    # ---- e2e through the public API with host buffers ---------------------------------------
     e2e = None
     if ws == 1 and args.e2e_steps > 0:
-        host_in = w.make_input().pin_memory() if args.host_input else torch.empty(w.shape, dtype=w.dtype).pin_memory()
+        host_in = w.make_input().pin_memory()
         host_out = torch.empty(prog.out_shape(w.shape), dtype=w.dtype).pin_memory()
+
+        def timed(step_fn):
+            step_fn()
+            torch.cuda.synchronize()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(args.e2e_steps):
+                step_fn()
+            f1.record(stream)
+            torch.cuda.synchronize()
+            return f0.elapsed_time(f1) / args.e2e_steps
+
+        # (1) the multi-sweep call (basalto.sweeps -> bst_stencil_sweeps), host in and out
+        ea = torch.empty(w.shape, dtype=w.dtype, device=dev)
+        eb = torch.empty_like(ea)
+
+        def e2e_api():
+            ea.copy_(host_in, non_blocking=True)
+            if prog.boundary == "zero":
+                res = basalto.sweeps(prog, ea, eb, sweeps)
+            else:
+                res = basalto.apply(prog, ea)
+            host_out.copy_(res, non_blocking=True)
+
+        e_ms = timed(e2e_api)
+        e2e = {"value": round(w.points * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
+               "h2d_bytes_per_step": w.points * es, "d2h_bytes_per_step": w.out_points * es,
+               "ms_per_step": round(e_ms, 3),
+               "path": "basalto.sweeps (C ABI bst_stencil_sweeps), pinned host grid copied in and out each step"}
+        # (2) the drop-in plugin: torch.compile(backend="basalto") called once per sweep
         torch._dynamo.reset()
         cf = torch.compile(w.fn, backend="basalto")
 
-        def e2e_step():
+        def e2e_plugin():
             x = host_in.to(dev, non_blocking=True)
             for _ in range(sweeps):
                 x = cf(x)
             host_out.copy_(x, non_blocking=True)
 
-        e2e_step()
-        torch.cuda.synchronize()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        f1.record(stream)
-        torch.cuda.synchronize()
-        e_ms = f0.elapsed_time(f1) / args.e2e_steps
-        e2e = {"value": round(w.points * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
-               "h2d_bytes_per_step": w.points * es, "d2h_bytes_per_step": w.out_points * es, "ms_per_step": round(e_ms, 3),
-               "path": "torch.compile(backend='basalto'), one call per sweep, pinned host buffers"}
+        p_ms = timed(e2e_plugin)
+        e2e["torch_compile_per_sweep"] = {"value": round(w.points * sweeps / (p_ms * 1e-3) / 1e9, 4),
+                                          "ms_per_step": round(p_ms, 3)}
 
     # ---- CPU baseline (rank 0, N = 1 only, bounded sample) ------------------------------------
     cpu = None
@@ -361,7 +383,7 @@ def run_basalto(args):
                          "traffic": _traffic(w.name, "march_tma_kernel"),
                          "algorithmic_bytes_per_launch": per_launch_bytes, "avg_launch_ms": round(launch_ms, 5)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-            "launches_expected": int(launches_per_step * args.steps),
+            "sweeps_per_launch": round(sweeps * args.steps / max(1, launches), 3),
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -7,6 +7,7 @@
 // operations in the same order, so the choice never changes a result bit.
 #pragma once
 #include "bst_launch.cuh"
+#include "bst_tb2d.cuh"
 
 namespace bst {
 
@@ -135,6 +136,92 @@ int dispatch_sweep(const LaunchReq& r) {
   if (shape_matches<Box<2, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, 4, 1, 2>>(r);
   if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, true>>>(r);
   return launch_direct_table<T>(r);
+}
+
+// ---- temporally blocked multi-sweep (2-D window shapes) -------------------------------
+template <typename T, class C>
+bool tb_eligible(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  if (c.ndim != 2 || c.boundary != BST_BOUNDARY_ZERO) return false;
+  if (reinterpret_cast<uintptr_t>(r.x) % 16 != 0 || r.xs[2] != 1 || (r.xs[0] * E) % 16 != 0) return false;
+  if (c.n[0] >= (int64_t(1) << 31) || c.n[2] >= (int64_t(1) << 31)) return false;
+  if (c.R[0] > C::R || c.R[2] > C::RX) return false;
+  return true;
+}
+
+template <typename T, class C>
+int launch_tb2d(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  const long long nm = r.m_hi - r.m_lo;
+  if (nm <= 0) return BST_OK;
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {cuuint64_t(c.n[2]), 1, cuuint64_t(c.n[0])};
+  const cuuint64_t strides[2] = {cuuint64_t(r.xs[0] * E), cuuint64_t(r.xs[0] * E)};
+  const cuuint32_t box[3] = {cuuint32_t(C::TXL), 1, cuuint32_t(C::RB)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  CUresult cr = enc(&map, tma_dtype<T>(), 3, const_cast<void*>(r.x), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(cr)) + ")");
+  auto kern = march_tb2d_kernel<T, C>;
+  TbArgs a{};
+  a.g = make_grid(r);
+  a.tiles_x = int((c.no[2] + C::TXO - 1) / C::TXO);
+  const int occ = occupancy(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
+  if (occ <= 0) return fail(BST_ERR_CUDA, "temporally blocked kernel does not fit on an SM");
+  const long long resident = (long long)occ * sm_count();
+  long long nchunks = 1;
+  choose_chunks(a.tiles_x, nm, 1, 2 * C::K * C::R + C::RB + 8, resident, &a.chunk, &nchunks);
+  a.n_items = (long long)a.tiles_x * nchunks;
+  a.err = device_error_word();
+  if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
+  a.vec_store = (reinterpret_cast<uintptr_t>(r.y) % 16 == 0 && r.ys[2] == 1 && (r.ys[0] * E) % 16 == 0) ? 1 : 0;
+  const long long grid = a.n_items < resident ? a.n_items : resident;
+  kern<<<unsigned(grid), C::THREADS, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
+                                                      make_coefs<T, C::shape::NTERMS>(c));
+  BST_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+#ifndef BST_TB_RB
+#define BST_TB_RB 4
+#endif
+#ifndef BST_TB_NSX
+#define BST_TB_NSX 4
+#endif
+template <typename T, class S, int K>
+using CfgTb = TbCfg<T, S, K, BST_TB_RB, BST_TB_NSX>;
+
+// Largest number of sweeps one temporally blocked launch can fuse for this request (1 = none).
+template <typename T>
+int tb_max_sweeps(const LaunchReq& r) {
+  if (shape_matches<Jacobi2D>(*r.c) && tb_eligible<T, CfgTb<T, Jacobi2D, 2>>(r)) return sizeof(T) == 4 ? 5 : 3;
+  return 1;
+}
+
+// k sweeps (2 <= k <= tb_max_sweeps) in one launch.
+template <typename T>
+int dispatch_tb(const LaunchReq& r, int k) {
+  if (shape_matches<Jacobi2D>(*r.c)) {
+    switch (k) {
+      case 2: return launch_tb2d<T, CfgTb<T, Jacobi2D, 2>>(r);
+      case 3: return launch_tb2d<T, CfgTb<T, Jacobi2D, 3>>(r);
+      case 4:
+        if constexpr (sizeof(T) == 4) return launch_tb2d<T, CfgTb<T, Jacobi2D, 4>>(r);
+        break;
+      case 5:
+        if constexpr (sizeof(T) == 4) return launch_tb2d<T, CfgTb<T, Jacobi2D, 5>>(r);
+        break;
+      default:
+        break;
+    }
+  }
+  return fail(BST_ERR_UNSUPPORTED, "no temporally blocked kernel for this request");
 }
 
 }  // namespace bst

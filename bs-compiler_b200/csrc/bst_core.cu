@@ -203,6 +203,12 @@ int dispatch_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, co
                  int64_t m_lo, int64_t m_hi, cudaStream_t st);
 int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
                  int64_t m_lo, int64_t m_hi, cudaStream_t st);
+int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
+int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
+int dispatch_tb_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
+                    cudaStream_t st);
+int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
+                    cudaStream_t st);
 
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
                  const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st) {
@@ -358,6 +364,40 @@ int bst_stencil_sweeps(const bst_program* prog, int32_t dtype, int32_t ndim, con
   int64_t st_t[3], s[3];
   contiguous_strides(ndim, shape, st_t);
   logical_strides(ndim, st_t, s);
+  // Fuse up to kmax sweeps per launch (temporal blocking) where a kernel exists; keep the
+  // number of launches of the same parity as nsteps so the result lands in the buffer the
+  // contract names.
+  const int kmax = dtype == BST_F32 ? tb_max_f32(c, a, s, b, s) : tb_max_f64(c, a, s, b, s);
+  if (kmax >= 2 && nsteps >= 2) {
+    int left = nsteps;
+    std::vector<int> ks;
+    while (left > 0) {
+      const int k = left < kmax ? left : kmax;
+      ks.push_back(k);
+      left -= k;
+    }
+    if ((int(ks.size()) & 1) != (nsteps & 1)) {
+      // split the last launch of two or more sweeps into two launches
+      for (int i = int(ks.size()) - 1; i >= 0; --i)
+        if (ks[i] >= 2) {
+          const int k = ks[i];
+          ks[i] = k - 1;
+          ks.insert(ks.begin() + i + 1, 1);
+          break;
+        }
+    }
+    void* src = a;
+    void* dst = b;
+    for (int k : ks) {
+      if (k == 1) rc = launch_sweep(c, dtype, src, s, dst, s, 0, c.no[0], static_cast<cudaStream_t>(stream));
+      else
+        rc = dtype == BST_F32 ? dispatch_tb_f32(c, src, s, dst, s, k, static_cast<cudaStream_t>(stream))
+                              : dispatch_tb_f64(c, src, s, dst, s, k, static_cast<cudaStream_t>(stream));
+      if (rc) return rc;
+      std::swap(src, dst);
+    }
+    return BST_OK;
+  }
   void* src = a;
   void* dst = b;
   for (int i = 0; i < nsteps; ++i) {

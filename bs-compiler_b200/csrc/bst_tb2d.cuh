@@ -1,0 +1,295 @@
+// bst_tb2d.cuh — temporally blocked 2-D march: K sweeps of a 2-D window stencil per launch.
+//
+// A multi-sweep run of a 2-D stencil reads and writes the whole grid once per sweep.  This
+// kernel keeps K successive sweeps in flight inside one pass over the grid, so HBM is read
+// and written once per K sweeps.  The arithmetic is unchanged (every level performs the
+// same separately rounded operations in the same order), so the result is bit-identical
+// to K single sweeps.
+//
+//  * Rows (the marching axis): one warp marches down a column strip.  Level 0 is the input
+//    (a register window of 2R+1 row vectors fed by TMA, as in march_tma_kernel); level l
+//    computes row i - l*R from level l-1's window and pushes it into its own window.  Level
+//    K is stored.  An item of output rows [mb, me) reads input rows [mb-K*R, me+K*R): the
+//    K*R halo rows on each side are recomputed by the neighbouring items.
+//  * Columns: the warp's 32 lanes own 128 (fp32) / 64 (fp64) columns, but only the central
+//    30 lanes' columns are stored.  Level l's values near the warp edges have no neighbour
+//    lane to take their x-halo from; the error moves inward by R columns per level and never
+//    reaches the stored columns while (K-1)*R <= one lane's width.
+//  * Dirichlet-0: level values outside the grid (rows or columns) are ghost cells of the
+//    next level and are forced to zero, exactly as a sweep reads zeros outside the grid.
+#pragma once
+#include "bst_kernels.cuh"
+
+namespace bst {
+
+template <typename T, class S, int K_, int RB_, int NSX_>
+struct TbCfg {
+  using shape = S;
+  static constexpr int K = K_;
+  static constexpr int VX = 16 / int(sizeof(T));
+  static constexpr int R = S::RM;                       // row radius
+  static constexpr int RX = S::RX;                      // column radius
+  static constexpr int HL = 1;                          // overlap lanes at each warp edge
+  static constexpr int TXO = (32 - 2 * HL) * VX;        // stored columns per tile
+  static constexpr int HXI = ((RX + VX - 1) / VX) * VX; // loaded columns beyond the warp
+  static constexpr int TXL = 32 * VX + 2 * HXI;         // loaded columns per row
+  static constexpr int RB = RB_;                        // rows per stage
+  static constexpr int PLANE = TXL;
+  static constexpr int STAGE_BYTES = round_up_c(PLANE * RB * int(sizeof(T)), 128);
+  static constexpr int STAGE = STAGE_BYTES / int(sizeof(T));
+  static constexpr int B = (R + RB - 1) / RB;            // earlier stages a group still reads
+  // A group waits for its own stage before the barrier and refills after it, so that
+  // stage must have been issued by the previous group: NS >= B + 2.
+  static constexpr int NS = (B + 2 > B + 1 + NSX_) ? B + 2 : B + 1 + NSX_;
+  static constexpr int SMEM = NS * STAGE_BYTES + 128;
+  static constexpr int SEGW = VX + 2 * HXI;
+  static constexpr int THREADS = 32;
+  static_assert(window_mode<S>() && S::RY == 0, "2-D window shapes only");
+  static_assert((K - 1) * RX <= HL * VX, "stored columns stay valid through K levels");
+  static_assert(TXL <= 256 && RB <= 256, "TMA box extent");
+  static_assert(NS >= B + 2, "every stage is issued before a group waits on it");
+};
+
+struct TbArgs {
+  GridDesc g;
+  int tiles_x, chunk;
+  long long n_items;
+  unsigned* err;
+  int vec_store;
+};
+
+template <typename T, class C, int V>
+struct TbFetch {
+  const T (&w)[2 * C::R + 1][C::VX];
+  const T (&seg)[C::SEGW];
+  template <int dm, int dy, int dx>
+  __device__ __forceinline__ T get() const {
+    if constexpr (dm != 0) return w[C::R + dm][V];
+    else return seg[C::HXI + V + dx];
+  }
+};
+
+// x-halo of one level's centre row: own vector plus neighbour lanes' elements; at level 0
+// the warp's edge lanes read the loaded halo columns from shared memory.
+template <typename T, class C, bool LEVEL0>
+__device__ __forceinline__ void tb_segment(T (&seg)[C::SEGW], const T (&own)[C::VX], const T* row, int lane) {
+#pragma unroll
+  for (int e = 0; e < C::VX; ++e) seg[C::HXI + e] = own[e];
+#pragma unroll
+  for (int e = -C::RX; e < 0; ++e) {
+    const int d = (-e + C::VX - 1) / C::VX;
+    T v = __shfl_up_sync(0xffffffffu, own[e + d * C::VX], d);
+    if (LEVEL0 && lane < d) v = row[e];
+    seg[C::HXI + e] = v;
+  }
+#pragma unroll
+  for (int e = C::VX; e < C::VX + C::RX; ++e) {
+    const int d = e / C::VX;
+    T v = __shfl_down_sync(0xffffffffu, own[e - d * C::VX], d);
+    if (LEVEL0 && lane >= 32 - d) v = row[e];
+    seg[C::HXI + e] = v;
+  }
+}
+
+template <typename T, class C, int... Vs>
+__device__ __forceinline__ void tb_eval(const T (&w)[2 * C::R + 1][C::VX], const T (&seg)[C::SEGW],
+                                        const Coefs<T, C::shape::NTERMS>& c, T (&res)[C::VX],
+                                        std::integer_sequence<int, Vs...>) {
+  ((res[Vs] = eval_shape<typename C::shape, T>(TbFetch<T, C, Vs>{w, seg}, c)), ...);
+}
+
+template <typename T, class C>
+__device__ __forceinline__ void tb_push(T (&w)[2 * C::R + 1][C::VX], const T (&v)[C::VX]) {
+#pragma unroll
+  for (int k = 0; k < 2 * C::R; ++k)
+#pragma unroll
+    for (int e = 0; e < C::VX; ++e) w[k][e] = w[k + 1][e];
+#pragma unroll
+  for (int e = 0; e < C::VX; ++e) w[2 * C::R][e] = v[e];
+}
+
+// Per-item constants of a tile.
+struct TbTile {
+  long long L0;      // first input row of the item
+  long long mb, me;  // stored output rows
+  int cmask;         // bit e: this lane's column e lies inside the grid
+  bool edge;         // the warp's columns reach outside the grid
+  bool store_lane;   // this lane's columns are stored
+  int c0;            // first column of this lane
+};
+
+// One step: consume input row `rel` (relative to L0); compute and push levels 1..K.
+template <typename T, class C, int L>
+__device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], const T* edge_row, int lane,
+                                          const TbTile& t, long long i, const Coefs<T, C::shape::NTERMS>& coef,
+                                          const GridDesc& g, T* __restrict__ out, int vec_store) {
+  if constexpr (L <= C::K) {
+    T seg[C::SEGW];
+    tb_segment<T, C, L == 1>(seg, win[L - 1][C::R], edge_row, lane);
+    T res[C::VX];
+    tb_eval<T, C>(win[L - 1], seg, coef, res, std::make_integer_sequence<int, C::VX>{});
+    const long long row = i - (long long)L * C::R;  // grid row this level computed
+    if constexpr (L < C::K) {
+      const bool row_in = row >= 0 && row < g.no[0];
+#pragma unroll
+      for (int e = 0; e < C::VX; ++e)
+        if (!row_in || (t.edge && !((t.cmask >> e) & 1))) res[e] = T(0);  // ghost cells of level L+1
+      tb_push<T, C>(win[L], res);
+      tb_levels<T, C, L + 1>(win, edge_row, lane, t, i, coef, g, out, vec_store);
+    } else {
+      if (row >= t.mb && row < t.me && t.store_lane) {
+        T* dst = out + row * g.so[0] + (long long)t.c0 * g.so[2];
+        if (vec_store && t.c0 + C::VX <= g.no[2]) {
+          using VT = typename Vec16<T>::type;
+          VT q;
+          T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+          for (int v = 0; v < C::VX; ++v) e[v] = res[v];
+          *reinterpret_cast<VT*>(dst) = q;
+        } else {
+#pragma unroll
+          for (int v = 0; v < C::VX; ++v)
+            if (t.c0 + v < g.no[2]) dst[(long long)v * g.so[2]] = res[v];
+        }
+      }
+    }
+  }
+}
+
+template <typename T, class C, int P>
+__device__ __forceinline__ void tb_step(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
+                                        const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
+                                        const GridDesc& g, T* __restrict__ out, int vec_store) {
+  const int s = grp * C::RB + P;  // input row relative to L0
+  if (s >= total) return;
+  const int col = C::HXI + lane * C::VX;
+  // Leading input row into level 0's window.
+  {
+    T v[C::VX];
+    lds_vec<T, C::VX>(sb[C::B] + P * C::PLANE + col, v);
+    tb_push<T, C>(win[0], v);
+  }
+  if (s < 2 * C::R) return;  // level 0's window is still filling
+  // Level 0's centre row (s - R) for the warp-edge x-halo; stage offset is compile-time.
+  constexpr int REL = P - C::R;                           // relative to this group's first row
+  constexpr int SK = REL >= 0 ? REL / C::RB : -((-REL + C::RB - 1) / C::RB);
+  constexpr int OFF = REL - SK * C::RB;
+  const T* edge_row = sb[C::B + SK] + OFF * C::PLANE + col;
+  tb_levels<T, C, 1>(win, edge_row, lane, t, t.L0 + s, coef, g, out, vec_store);
+}
+
+template <typename T, class C, int... Ps>
+__device__ __forceinline__ void tb_group(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
+                                         const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
+                                         const GridDesc& g, T* __restrict__ out, int vec_store,
+                                         std::integer_sequence<int, Ps...>) {
+  (tb_step<T, C, Ps>(win, sb, lane, t, grp, total, coef, g, out, vec_store), ...);
+}
+
+template <typename T, class C>
+__global__ void __launch_bounds__(32)
+    march_tb2d_kernel(const __grid_constant__ CUtensorMap tmap, T* __restrict__ out, const TbArgs a,
+                      const Coefs<T, C::shape::NTERMS> coef) {
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t bars[C::NS];
+  T* ring = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int lane = threadIdx.x;
+  const bool leader = lane == 0;
+  if (leader) {
+    for (int i = 0; i < C::NS; ++i) mbar_init(&bars[i], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const GridDesc& g = a.g;
+  unsigned q_base = 0;
+  int n_issued = 0, n_waited = 0;
+  bool failed = false;
+  T win[C::K][2 * C::R + 1][C::VX];
+
+  for (long long item = blockIdx.x; item < a.n_items; item += gridDim.x) {
+    const int tile_x = int(item % a.tiles_x);
+    const int chunk = int(item / a.tiles_x);
+    const int x0 = tile_x * C::TXO;
+    TbTile t;
+    t.mb = g.m_lo + (long long)chunk * a.chunk;
+    t.me = (t.mb + a.chunk < g.m_hi) ? t.mb + a.chunk : g.m_hi;
+    t.L0 = t.mb - (long long)C::K * C::R;
+    t.c0 = x0 - C::HL * C::VX + lane * C::VX;
+    t.cmask = 0;
+#pragma unroll
+    for (int e = 0; e < C::VX; ++e)
+      if (t.c0 + e >= 0 && t.c0 + e < g.no[2]) t.cmask |= 1 << e;
+    t.edge = (x0 - C::HL * C::VX < 0) || (x0 - C::HL * C::VX + 32 * C::VX > g.no[2]);
+    t.store_lane = lane >= C::HL && lane < 32 - C::HL && t.c0 < g.no[2];
+    const int total = int(t.me - t.mb) + 2 * C::K * C::R;  // input rows of the item
+    const int ngroups = (total + C::RB - 1) / C::RB;
+    const int qt = ngroups;
+    const int cx = x0 - C::HL * C::VX - C::HXI;
+    const int L0 = int(t.L0);
+    auto issue = [&](int q) {
+      const unsigned slot = (q_base + unsigned(q)) % C::NS;
+      mbar_expect_tx(&bars[slot], unsigned(C::PLANE * C::RB * sizeof(T)));
+      tma_load_3d(ring + size_t(slot) * C::STAGE, &tmap, &bars[slot], cx, 0, L0 + q * C::RB);
+    };
+    __syncthreads();
+    n_issued = qt < C::NS ? qt : C::NS;
+    n_waited = 0;
+    if (leader) {
+      fence_proxy_async_smem();
+      for (int q = 0; q < n_issued; ++q) issue(q);
+    }
+#pragma unroll
+    for (int l = 0; l < C::K; ++l)
+#pragma unroll
+      for (int k = 0; k < 2 * C::R + 1; ++k)
+#pragma unroll
+        for (int e = 0; e < C::VX; ++e) win[l][k][e] = T(0);
+
+    for (int grp = 0; grp < ngroups; ++grp) {
+      for (; n_waited <= grp; ++n_waited) {
+        const unsigned gq = q_base + unsigned(n_waited);
+        if (!failed && !mbar_wait_bounded(&bars[gq % C::NS], (gq / C::NS) & 1u)) failed = true;
+      }
+      if (__syncthreads_or(failed)) {
+        failed = true;
+        break;
+      }
+      if (grp >= 1) {
+        const int lim = grp - C::B + C::NS;  // stages before grp - B are retired
+        const int target = qt < lim ? qt : lim;
+        if (n_issued < target) {
+          if (leader) {
+            fence_proxy_async_smem();
+            for (int q = n_issued; q < target; ++q) issue(q);
+          }
+          n_issued = target;
+        }
+      }
+      const T* sb[C::B + 1];  // stages grp-B .. grp (earlier ones only for the edge halo rows)
+#pragma unroll
+      for (int k = 0; k <= C::B; ++k) {
+        const int q = grp - C::B + k;
+        sb[k] = ring + size_t((q_base + unsigned(q < 0 ? 0 : q)) % C::NS) * C::STAGE;
+      }
+      tb_group<T, C>(win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
+                     std::make_integer_sequence<int, C::RB>{});
+    }
+    if (failed) break;
+    q_base += unsigned(qt);
+  }
+
+  if (failed) {
+    if (leader) {
+      atomicOr(a.err, kErrTmaTimeout);
+      for (int q = n_waited; q < n_issued; ++q) {
+        const unsigned gq = q_base + unsigned(q);
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(&bars[gq % C::NS], (gq / C::NS) & 1u) && global_ns() - t0 < 200000000ull) {
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace bst

@@ -214,3 +214,25 @@ def test_valid_region_3d_fast_path():
         x = torch.randn(shape, generator=torch.Generator().manual_seed(9))
         ref = O.eval_program(x.numpy(), oracle_terms(prog), boundary="valid", shrink=(2, 2, 2))
         assert np.array_equal(b.apply(prog, x.cuda()).cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("dtype,shape", [(torch.float32, (257, 300)), (torch.float32, (64, 1024)),
+                                         (torch.float32, (3, 124)), (torch.float64, (129, 130)),
+                                         (torch.float64, (70, 512)), (torch.float32, (1000, 120))])
+def test_temporally_blocked_sweeps_match_oracle(dtype, shape):
+    """Multi-sweep 2-D runs fuse several sweeps per launch; every sweep count must give the
+    iterated single-sweep result bit for bit, in the buffer the sweeps contract names."""
+    b = _basalto()
+    from basalto import program as P
+    x = torch.rand(shape, dtype=dtype, generator=torch.Generator().manual_seed(17)) * 2 - 1
+    prog = P.jacobi5_2d()
+    for n in (2, 3, 4, 5, 6, 7, 10, 11, 12, 25):
+        a = x.cuda()
+        bb = torch.empty_like(a)
+        n0 = b.launch_count()
+        res = b.sweeps(prog, a, bb, n)
+        torch.cuda.synchronize()
+        assert (res.data_ptr() == bb.data_ptr()) == (n % 2 == 1)
+        ref = O.sweeps(x.numpy(), O.jacobi5_2d, n)
+        assert np.array_equal(res.cpu().numpy(), ref), (shape, dtype, n)
+        assert b.launch_count() - n0 < n  # sweeps were fused
