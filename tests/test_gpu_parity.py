@@ -235,4 +235,5 @@ def test_temporally_blocked_sweeps_match_oracle(dtype, shape):
         assert (res.data_ptr() == bb.data_ptr()) == (n % 2 == 1)
         ref = O.sweeps(x.numpy(), O.jacobi5_2d, n)
         assert np.array_equal(res.cpu().numpy(), ref), (shape, dtype, n)
-        assert b.launch_count() - n0 < n  # sweeps were fused
+        if n >= 3:  # two sweeps cannot fuse and still leave the result in buffer a
+            assert b.launch_count() - n0 < n  # sweeps were fused
