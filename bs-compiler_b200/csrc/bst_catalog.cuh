@@ -189,10 +189,10 @@ int launch_tb2d(const LaunchReq& r) {
 }
 
 #ifndef BST_TB_RB
-#define BST_TB_RB 4
+#define BST_TB_RB 6  // a multiple of the window (2R+1 = 3): one group body, no phase dispatch
 #endif
 #ifndef BST_TB_NSX
-#define BST_TB_NSX 4
+#define BST_TB_NSX 2
 #endif
 template <typename T, class S, int K>
 using CfgTb = TbCfg<T, S, K, BST_TB_RB, BST_TB_NSX>;

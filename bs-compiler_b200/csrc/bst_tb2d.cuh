@@ -58,13 +58,16 @@ struct TbArgs {
   int vec_store;
 };
 
-template <typename T, class C, int V>
+// Level windows are circular: a level that has been pushed c times keeps its logical row k
+// (0 = oldest of the 2R+1) in physical slot (c + k) mod W, so a push writes one slot and no
+// register moves.  Every push count is a compile-time function of the step's phase.
+template <typename T, class C, int V, int PH>  // PH = pushes of the window so far, mod W
 struct TbFetch {
   const T (&w)[2 * C::R + 1][C::VX];
   const T (&seg)[C::SEGW];
   template <int dm, int dy, int dx>
   __device__ __forceinline__ T get() const {
-    if constexpr (dm != 0) return w[C::R + dm][V];
+    if constexpr (dm != 0) return w[(PH + C::R + dm) % (2 * C::R + 1)][V];
     else return seg[C::HXI + V + dx];
   }
 };
@@ -91,21 +94,11 @@ __device__ __forceinline__ void tb_segment(T (&seg)[C::SEGW], const T (&own)[C::
   }
 }
 
-template <typename T, class C, int... Vs>
+template <typename T, class C, int PH, int... Vs>
 __device__ __forceinline__ void tb_eval(const T (&w)[2 * C::R + 1][C::VX], const T (&seg)[C::SEGW],
                                         const Coefs<T, C::shape::NTERMS>& c, T (&res)[C::VX],
                                         std::integer_sequence<int, Vs...>) {
-  ((res[Vs] = eval_shape<typename C::shape, T>(TbFetch<T, C, Vs>{w, seg}, c)), ...);
-}
-
-template <typename T, class C>
-__device__ __forceinline__ void tb_push(T (&w)[2 * C::R + 1][C::VX], const T (&v)[C::VX]) {
-#pragma unroll
-  for (int k = 0; k < 2 * C::R; ++k)
-#pragma unroll
-    for (int e = 0; e < C::VX; ++e) w[k][e] = w[k + 1][e];
-#pragma unroll
-  for (int e = 0; e < C::VX; ++e) w[2 * C::R][e] = v[e];
+  ((res[Vs] = eval_shape<typename C::shape, T>(TbFetch<T, C, Vs, PH>{w, seg}, c)), ...);
 }
 
 // Per-item constants of a tile.
@@ -118,24 +111,36 @@ struct TbTile {
   int c0;            // first column of this lane
 };
 
-// One step: consume input row `rel` (relative to L0); compute and push levels 1..K.
-template <typename T, class C, int L>
+// Levels L..K for input row i.  Q0 = (pushes of level 0 so far, this step's included) mod W;
+// window l >= 1 has then been pushed Q0 - 2R times (mod W) when it is read, and this step's
+// row of level l goes to slot (Q0 - 1 - 2R) mod W.
+template <typename T, class C, int L, int Q0>
 __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], const T* edge_row, int lane,
                                           const TbTile& t, long long i, const Coefs<T, C::shape::NTERMS>& coef,
                                           const GridDesc& g, T* __restrict__ out, int vec_store) {
   if constexpr (L <= C::K) {
+    constexpr int W = 2 * C::R + 1;
+    constexpr int PH = L == 1 ? Q0 % W : ((Q0 - 2 * C::R) % W + W) % W;  // pushes of window L-1, mod W
     T seg[C::SEGW];
-    tb_segment<T, C, L == 1>(seg, win[L - 1][C::R], edge_row, lane);
+    tb_segment<T, C, L == 1>(seg, win[L - 1][(PH + C::R) % W], edge_row, lane);
     T res[C::VX];
-    tb_eval<T, C>(win[L - 1], seg, coef, res, std::make_integer_sequence<int, C::VX>{});
+    tb_eval<T, C, PH>(win[L - 1], seg, coef, res, std::make_integer_sequence<int, C::VX>{});
     const long long row = i - (long long)L * C::R;  // grid row this level computed
     if constexpr (L < C::K) {
-      const bool row_in = row >= 0 && row < g.no[0];
+      // Ghost cells of level L+1 are zero: rows outside the grid (warp-uniform), columns
+      // outside the grid (edge tiles only, warp-uniform branch).
+      if (row < 0 || row >= g.no[0]) {
 #pragma unroll
-      for (int e = 0; e < C::VX; ++e)
-        if (!row_in || (t.edge && !((t.cmask >> e) & 1))) res[e] = T(0);  // ghost cells of level L+1
-      tb_push<T, C>(win[L], res);
-      tb_levels<T, C, L + 1>(win, edge_row, lane, t, i, coef, g, out, vec_store);
+        for (int e = 0; e < C::VX; ++e) res[e] = T(0);
+      } else if (t.edge) {
+#pragma unroll
+        for (int e = 0; e < C::VX; ++e)
+          if (!((t.cmask >> e) & 1)) res[e] = T(0);
+      }
+      constexpr int SLOT = ((Q0 - 1 - 2 * C::R) % W + W) % W;
+#pragma unroll
+      for (int e = 0; e < C::VX; ++e) win[L][SLOT][e] = res[e];
+      tb_levels<T, C, L + 1, Q0>(win, edge_row, lane, t, i, coef, g, out, vec_store);
     } else {
       if (row >= t.mb && row < t.me && t.store_lane) {
         T* dst = out + row * g.so[0] + (long long)t.c0 * g.so[2];
@@ -156,34 +161,44 @@ __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], c
   }
 }
 
-template <typename T, class C, int P>
+// Step P of a group whose first input row has phase GP = (grp * RB) mod W.
+template <typename T, class C, int GP, int P>
 __device__ __forceinline__ void tb_step(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
                                         const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
                                         const GridDesc& g, T* __restrict__ out, int vec_store) {
+  constexpr int W = 2 * C::R + 1;
   const int s = grp * C::RB + P;  // input row relative to L0
   if (s >= total) return;
   const int col = C::HXI + lane * C::VX;
-  // Leading input row into level 0's window.
-  {
-    T v[C::VX];
-    lds_vec<T, C::VX>(sb[C::B] + P * C::PLANE + col, v);
-    tb_push<T, C>(win[0], v);
-  }
+  // Leading input row into level 0's window: push number s goes to slot s mod W.
+  lds_vec<T, C::VX>(sb[C::B] + P * C::PLANE + col, win[0][(GP + P) % W]);
   if (s < 2 * C::R) return;  // level 0's window is still filling
   // Level 0's centre row (s - R) for the warp-edge x-halo; stage offset is compile-time.
-  constexpr int REL = P - C::R;                           // relative to this group's first row
+  constexpr int REL = P - C::R;  // relative to this group's first row
   constexpr int SK = REL >= 0 ? REL / C::RB : -((-REL + C::RB - 1) / C::RB);
   constexpr int OFF = REL - SK * C::RB;
   const T* edge_row = sb[C::B + SK] + OFF * C::PLANE + col;
-  tb_levels<T, C, 1>(win, edge_row, lane, t, t.L0 + s, coef, g, out, vec_store);
+  tb_levels<T, C, 1, (GP + P + 1) % W>(win, edge_row, lane, t, t.L0 + s, coef, g, out, vec_store);
 }
 
-template <typename T, class C, int... Ps>
+template <typename T, class C, int GP, int... Ps>
 __device__ __forceinline__ void tb_group(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
                                          const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
                                          const GridDesc& g, T* __restrict__ out, int vec_store,
                                          std::integer_sequence<int, Ps...>) {
-  (tb_step<T, C, Ps>(win, sb, lane, t, grp, total, coef, g, out, vec_store), ...);
+  (tb_step<T, C, GP, Ps>(win, sb, lane, t, grp, total, coef, g, out, vec_store), ...);
+}
+
+// Dispatch the group body on its phase (grp * RB) mod W (compile-time slot arithmetic).
+template <typename T, class C, int... GPs>
+__device__ __forceinline__ void tb_group_phase(int phase, T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb,
+                                               int lane, const TbTile& t, int grp, int total,
+                                               const Coefs<T, C::shape::NTERMS>& coef, const GridDesc& g,
+                                               T* __restrict__ out, int vec_store, std::integer_sequence<int, GPs...>) {
+  ((phase == GPs ? tb_group<T, C, GPs>(win, sb, lane, t, grp, total, coef, g, out, vec_store,
+                                       std::make_integer_sequence<int, C::RB>{})
+                 : void()),
+   ...);
 }
 
 template <typename T, class C>
@@ -271,8 +286,13 @@ __global__ void __launch_bounds__(32)
         const int q = grp - C::B + k;
         sb[k] = ring + size_t((q_base + unsigned(q < 0 ? 0 : q)) % C::NS) * C::STAGE;
       }
-      tb_group<T, C>(win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
-                     std::make_integer_sequence<int, C::RB>{});
+      constexpr int W = 2 * C::R + 1;
+      if constexpr (C::RB % W == 0)  // every group starts at phase 0: one body
+        tb_group<T, C, 0>(win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
+                          std::make_integer_sequence<int, C::RB>{});
+      else
+        tb_group_phase<T, C>((grp * C::RB) % W, win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
+                             std::make_integer_sequence<int, W>{});
     }
     if (failed) break;
     q_base += unsigned(qt);
