@@ -5,16 +5,18 @@
 
 Workload (default): 2-D five-point Jacobi, fp32 8192 x 8192 ~U(-1,1) seed 1, Dirichlet-0
 ghost cells, 100 ping-pong sweeps.  One step = the full 100-sweep run.  At N > 1 every rank
-owns an 8192 x 8192 slab of a (8192*N) x 8192 grid split along rows (weak scaling): each
-sweep exchanges one ghost row with each neighbour over NCCL, overlapped with the interior.
+owns an 8192 x 8192 slab of a (8192*N) x 8192 grid split along rows (weak scaling), with
+deep ghosts: every fused pass of k sweeps exchanges k ghost rows with each neighbour over
+NCCL, overlapped with the interior.
 
 value      grid-point updates per second of the whole job (Gpts/s), inputs resident in HBM,
            CUDA events on the compute stream, max over ranks.
 e2e        the same metric through the public plugin path: pinned host grid -> H2D ->
            torch.compile(jacobi, backend="basalto") called once per sweep -> D2H, all inside
-           the timed region (N = 1; at N > 1 the slab API with host copies).
+           the timed region (N = 1; at N > 1 the slab API, bst_halo_exchange +
+           bst_slab_sweeps_deep, with each rank's slab copied in and out).
 roofline   the Jacobi kernel: algorithmic bytes (8 B per point: one read + one write) per
-           launch / average launch time, against the measured HBM copy bandwidth.
+           pass over the grid / average pass time, against the measured HBM copy bandwidth.
 cpu_baseline / --impl reference
            the reference's CPU path: eager torch through the reference backend's control
            flow (oracle/reference_path.py), all host threads, a bounded number of sweeps.
@@ -119,6 +121,28 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class EnergyMeter:
+    """NVML total-energy counter (millijoules since driver load) read around the timed region."""
+
+    def __init__(self, index: int):
+        self.nv = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.nv = pynvml
+        except Exception:
+            self.nv = None
+
+    def read(self):
+        if self.nv is None:
+            return None
+        try:
+            return float(self.nv.nvmlDeviceGetTotalEnergyConsumption(self.h))
+        except Exception:
+            return None
 
 
 def _dist():
@@ -236,13 +260,17 @@ def run_basalto(args):
         points_job = w.points
         comm = None
     else:
-        # Weak scaling: each rank owns a full-size slab; ghost planes along axis 0.
+        # Weak scaling: each rank owns a full-size slab; deep ghost planes along axis 0 (the
+        # fused kernel's k x radius, so one exchange per k sweeps).
+        from basalto.slab import fuse_plan, slab_ghost_depth
         R = prog.radius()[0]
         local_shape = list(w.shape)
+        dt = _abi.BST_F32 if w.dtype == torch.float32 else _abi.BST_F64
+        G = slab_ghost_depth(prog, [local_shape[0] * ws] + local_shape[1:], ws, dt)
         g = torch.Generator(device=dev).manual_seed(w.seed + 1000 * rank)
-        a = torch.zeros([local_shape[0] + 2 * R] + local_shape[1:], dtype=w.dtype, device=dev)
+        a = torch.zeros([local_shape[0] + 2 * G] + local_shape[1:], dtype=w.dtype, device=dev)
         b = torch.zeros_like(a)
-        a[R:R + local_shape[0]].copy_(torch.rand(local_shape, generator=g, dtype=w.dtype, device=dev) * 2 - 1)
+        a[G:G + local_shape[0]].copy_(torch.rand(local_shape, generator=g, dtype=w.dtype, device=dev) * 2 - 1)
         uid = (ctypes.c_uint8 * 128)()
         obj = [None]
         if rank == 0:
@@ -254,19 +282,20 @@ def run_basalto(args):
         _abi.check(_abi.lib().bst_comm_create(uid, ws, rank, local, 120.0, ctypes.byref(h)))
         comm = h
         cp = prog.to_c(local_shape)
-        dt = _abi.BST_F32 if w.dtype == torch.float32 else _abi.BST_F64
         plane = 1
         for s in local_shape[1:]:
             plane *= s
         sp = ctypes.c_void_p(stream.cuda_stream)
-        _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0], R, sp))
+        _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0], G, sp))
         shp = _abi.i64_array(local_shape)
 
         def step():
-            _abi.check(_abi.lib().bst_slab_sweeps(comm, ctypes.byref(cp), dt, len(local_shape), shp,
-                                                  ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
-                                                  sweeps, sp))
+            _abi.check(_abi.lib().bst_slab_sweeps_deep(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
+                                                       ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
+                                                       sweeps, sp))
 
+        # Passes over the slab per step (each pass = boundary launches + interior launch).
+        slab_passes = len(fuse_plan(sweeps, G // R if R else 1))
         points_job = w.points * ws
 
     # ---- timed region (device time, CUDA events on the compute stream) -------------------
@@ -277,6 +306,8 @@ def run_basalto(args):
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    energy = EnergyMeter(local)
+    mj0 = energy.read()
     n0 = basalto.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -290,8 +321,14 @@ def run_basalto(args):
     if dist:
         dist.barrier()
     launches = basalto.launch_count() - n0
+    mj1 = energy.read()
     clk = clocks.stop()
     ms_total = e0.elapsed_time(e1)
+    joules = (mj1 - mj0) / 1e3 if mj0 is not None and mj1 is not None else float("nan")
+    if dist:
+        t = torch.tensor([joules], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        joules = float(t.item())
     if dist:
         t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -303,10 +340,19 @@ def run_basalto(args):
     # Multi-sweep runs fuse several sweeps per launch (temporal blocking); each launch still
     # reads its input grid once and writes its output once, so the algorithmic traffic of a
     # launch is 2 * elem bytes per point whatever the number of sweeps it fuses.
-    launch_ms = ms_total / max(1, launches)  # this rank's launches over the timed region
+    # At N > 1 a pass over the slab is split into boundary and interior launches: the unit is
+    # the pass (all of this rank's points once), timed over the whole region.
+    passes = launches if ws == 1 else slab_passes * args.steps
+    launch_ms = ms_total / max(1, passes)
     per_launch_bytes = 2 * es * w.points
     achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
     peak, peak_src = _peaks()
+    if w.name.startswith("mean3"):
+        kernel = "line_kernel"
+    elif sweeps * args.steps > passes:
+        kernel = "march_tb2d_kernel"  # several sweeps fused per pass
+    else:
+        kernel = "march_tma_kernel"
 
     # ---- e2e through the public API with host buffers ---------------------------------------
     e2e = None
@@ -356,6 +402,62 @@ def run_basalto(args):
         e2e["torch_compile_per_sweep"] = {"value": round(w.points * sweeps / (p_ms * 1e-3) / 1e9, 4),
                                           "ms_per_step": round(p_ms, 3)}
 
+    halo = None
+    if ws > 1:
+        # NVLink halo bandwidth: the ghost exchange alone, G planes each way per neighbour.
+        n_ex = 20
+        torch.cuda.synchronize()
+        dist.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for _ in range(n_ex):
+            _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0],
+                                                    G, sp))
+        h1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([h0.elapsed_time(h1) / n_ex], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ex_ms = float(t.item())
+        nbrs = min(2, ws - 1)  # an interior rank's neighbours (an end rank's at N = 2)
+        ex_bytes = 2 * nbrs * G * plane * es  # sent + received by that rank
+        halo = {"ghost_planes": G, "bytes_per_exchange": ex_bytes, "exchange_ms": round(ex_ms, 4),
+                "nvlink_gbs": round(ex_bytes / (ex_ms * 1e-3) / 1e9, 2),
+                "exchanges_per_step": slab_passes,
+                "note": "exchange timed alone (max over ranks); in the sweep loop it overlaps the interior launch"}
+
+    if ws > 1 and args.e2e_steps > 0:
+        # The slab API with host buffers: each step copies this rank's slab in from pinned host
+        # memory, exchanges ghosts, runs the sweeps and copies the owned result back.
+        host_in = (torch.rand(local_shape, generator=torch.Generator().manual_seed(w.seed + rank), dtype=w.dtype)
+                   * 2 - 1).pin_memory()
+        host_out = torch.empty(local_shape, dtype=w.dtype).pin_memory()
+        res = a if sweeps % 2 == 0 else b
+
+        def e2e_slab():
+            a[G:G + local_shape[0]].copy_(host_in, non_blocking=True)
+            _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0],
+                                                    G, sp))
+            step()
+            host_out.copy_(res[G:G + local_shape[0]], non_blocking=True)
+
+        e2e_slab()
+        torch.cuda.synchronize()
+        dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_slab()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([f0.elapsed_time(f1) / args.e2e_steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+        e2e = {"value": round(points_job * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
+               "h2d_bytes_per_step": w.points * es * ws, "d2h_bytes_per_step": w.points * es * ws,
+               "ms_per_step": round(e_ms, 3),
+               "path": "bst_halo_exchange + bst_slab_sweeps_deep per rank, pinned host slab copied in and out "
+                       "each step (bytes summed over ranks), max over ranks"}
+
     # ---- CPU baseline (rank 0, N = 1 only, bounded sample) ------------------------------------
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -380,9 +482,14 @@ def run_basalto(args):
                        "l2": f"inputs larger than L2 (2 x {w.points * es / 2**20:.0f} MiB ping-pong)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": _traffic(w.name, "march_tma_kernel"),
+                         "frac_of_nominal_8000": round(achieved / 8000.0, 4),
+                         "kernel": kernel, "traffic": _traffic(w.name, kernel),
                          "algorithmic_bytes_per_launch": per_launch_bytes, "avg_launch_ms": round(launch_ms, 5)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "energy": {"joules_per_step": round(joules / args.steps, 4),
+                       "gpts_per_joule": round(points_job * sweeps * args.steps / joules / 1e9, 3)}
+                      if joules == joules and joules > 0 else None,
+            "halo": halo,
             "sweeps_per_launch": round(sweeps * args.steps / max(1, launches), 3),
             "clocks": clk,
         }

@@ -93,6 +93,10 @@ SIGNATURES = [
     ("bst_halo_exchange", c_int32, [c_void_p, c_void_p, c_int32, c_int64, c_int64, c_int32, c_void_p]),
     ("bst_slab_sweeps", c_int32,
      [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_void_p, c_void_p, c_int32, c_void_p]),
+    ("bst_slab_ghost_depth", c_int32, [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), POINTER(c_int32)]),
+    ("bst_slab_sweeps_deep", c_int32,
+     [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
+      c_void_p]),
 ]
 
 _lib = None

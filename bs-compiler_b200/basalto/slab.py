@@ -14,8 +14,13 @@ extra planes on either side:
 Global ends are Dirichlet-0 (not periodic), so the sharded result equals the single-grid
 result point for point.  The exchange is one NCCL group of contiguous send/recv pairs (no
 packing), issued by the C library on its own stream and overlapped with the interior
-sweep (bst_slab_sweeps).  Plumbing (ranks, the NCCL unique id) goes through
+sweep (bst_slab_sweeps_deep).  Plumbing (ranks, the NCCL unique id) goes through
 torch.distributed.
+
+Deep halos: where a kernel fuses k sweeps per pass (temporal blocking), the ghost depth is
+k x radius and the slab exchanges once per k sweeps instead of once per sweep; the depth
+defaults to what the library reports for the program (bst_slab_ghost_depth), capped by the
+smallest rank's owned planes.
 """
 from __future__ import annotations
 
@@ -98,6 +103,42 @@ class SlabLayout:
                              f"{max(self.ghost, 1)} for a radius-{self.ghost} stencil")
 
 
+def fuse_plan(nsteps: int, kmax: int) -> list[int]:
+    """Sweeps per fused launch for nsteps ping-pong sweeps, as the C library plans them: at
+    most kmax per launch, with a launch count of nsteps' parity (the result then lands in the
+    buffer a per-sweep ping-pong would use)."""
+    if kmax < 2 or nsteps < 2:
+        return [1] * max(nsteps, 0)
+    ks = []
+    left = nsteps
+    while left:
+        ks.append(min(kmax, left))
+        left -= ks[-1]
+    if len(ks) % 2 != nsteps % 2:
+        for i in range(len(ks) - 1, -1, -1):
+            if ks[i] >= 2:
+                ks[i:i + 1] = [ks[i] - 1, 1]
+                break
+    return ks
+
+
+def slab_ghost_depth(program: StencilProgram, global_shape, nranks: int, dtype_code: int) -> int:
+    """Ghost planes per side for a slab run: the library's fused-sweep depth for this program
+    (a multiple of the axis-0 radius), capped by the smallest rank's owned planes.  Every rank
+    computes the same value from the same arguments."""
+    r = program.radius()[0]
+    smallest = min(partition(global_shape[0], nranks, k)[1] for k in range(nranks))
+    local = (smallest,) + tuple(global_shape[1:])
+    depth = ctypes.c_int32(0)
+    cprog = program.to_c(local)
+    _abi.check(_abi.lib().bst_slab_ghost_depth(ctypes.byref(cprog), dtype_code, len(local), _abi.i64_array(local),
+                                               ctypes.byref(depth)))
+    g = int(depth.value)
+    if nranks > 1 and r > 0 and g > smallest:
+        g = max(r, smallest // r * r)
+    return max(g, r)
+
+
 class SlabDomain:
     """A sharded grid on this rank's GPU with a ghost-exchanging sweep loop.
 
@@ -107,7 +148,7 @@ class SlabDomain:
     """
 
     def __init__(self, program: StencilProgram, global_shape, dtype=torch.float32, device=None,
-                 timeout_s: float = 120.0, group=None):
+                 timeout_s: float = 120.0, group=None, ghost: int | None = None):
         import torch.distributed as dist
 
         if program.boundary != "zero" or program.ndim not in (2, 3) or program.ndim != len(global_shape):
@@ -116,13 +157,18 @@ class SlabDomain:
         self.dtype = dtype
         ws = dist.get_world_size(group) if dist.is_initialized() else 1
         rank = dist.get_rank(group) if dist.is_initialized() else 0
-        self.layout = SlabLayout(tuple(int(s) for s in global_shape), ws, rank, program.radius()[0])
+        gshape = tuple(int(s) for s in global_shape)
+        self._dt = _abi.BST_F32 if dtype == torch.float32 else _abi.BST_F64
+        if ghost is None:
+            ghost = slab_ghost_depth(program, gshape, ws, self._dt)
+        self.layout = SlabLayout(gshape, ws, rank, int(ghost))
+        if self.layout.ghost < program.radius()[0]:
+            raise ValueError("ghost depth is below the program's axis-0 radius")
         self.layout.validate()
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.a = torch.zeros(self.layout.buffer_shape, dtype=dtype, device=self.device)
         self.b = torch.zeros_like(self.a)
         self._cprog = program.to_c(self.layout.local_shape)
-        self._dt = _abi.BST_F32 if dtype == torch.float32 else _abi.BST_F64
         obj = [None]
         if rank == 0:
             uid = (ctypes.c_uint8 * 128)()
@@ -161,9 +207,9 @@ class SlabDomain:
         L = self.layout
         other = self.b if self.current is self.a else self.a
         with torch.cuda.device(self.device):
-            _abi.check(_abi.lib().bst_slab_sweeps(
+            _abi.check(_abi.lib().bst_slab_sweeps_deep(
                 self._comm, ctypes.byref(self._cprog), self._dt, len(L.local_shape), _abi.i64_array(L.local_shape),
-                ctypes.c_void_p(self.current.data_ptr()), ctypes.c_void_p(other.data_ptr()), int(nsteps),
+                L.ghost, ctypes.c_void_p(self.current.data_ptr()), ctypes.c_void_p(other.data_ptr()), int(nsteps),
                 self._stream()))
         if nsteps % 2:
             self.current = other

@@ -143,7 +143,8 @@ template <typename T, class C>
 bool tb_eligible(const LaunchReq& r) {
   const Canon& c = *r.c;
   constexpr int E = sizeof(T);
-  if (c.ndim != 2 || c.boundary != BST_BOUNDARY_ZERO) return false;
+  if (c.ndim != 2 || c.boundary != BST_BOUNDARY_ZERO || c.org[2] != 0) return false;
+  if (c.no[0] >= (int64_t(1) << 30)) return false;
   if (reinterpret_cast<uintptr_t>(r.x) % 16 != 0 || r.xs[2] != 1 || (r.xs[0] * E) % 16 != 0) return false;
   if (c.n[0] >= (int64_t(1) << 31) || c.n[2] >= (int64_t(1) << 31)) return false;
   if (c.R[0] > C::R || c.R[2] > C::RX) return false;
@@ -180,6 +181,10 @@ int launch_tb2d(const LaunchReq& r) {
   a.err = device_error_word();
   if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
   a.vec_store = (reinterpret_cast<uintptr_t>(r.y) % 16 == 0 && r.ys[2] == 1 && (r.ys[0] * E) % 16 == 0) ? 1 : 0;
+  const int64_t big = int64_t(1) << 30;
+  const int64_t lo = r.row_hi < r.row_lo ? 0 : r.row_lo, hi = r.row_hi < r.row_lo ? c.no[0] : r.row_hi;
+  a.row_lo = int(lo < -big ? -big : lo);
+  a.row_hi = int(hi > big ? big : hi);
   const long long grid = a.n_items < resident ? a.n_items : resident;
   kern<<<unsigned(grid), C::THREADS, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
                                                       make_coefs<T, C::shape::NTERMS>(c));

@@ -206,15 +206,53 @@ int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, co
 int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
 int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
 int dispatch_tb_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
-                    cudaStream_t st);
+                    int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
-                    cudaStream_t st);
+                    int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
                  const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st) {
   if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st);
   if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st);
   return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+}
+
+int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]) {
+  if (dtype == BST_F32) return tb_max_f32(c, x, xs, y, ys);
+  if (dtype == BST_F64) return tb_max_f64(c, x, xs, y, ys);
+  return 1;
+}
+
+int launch_fused(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
+                 int k, int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st) {
+  if (k == 1) return launch_sweep(c, dtype, x, xs, y, ys, m_lo, m_hi, st);
+  if (dtype == BST_F32) return dispatch_tb_f32(c, x, xs, y, ys, k, m_lo, m_hi, row_lo, row_hi, st);
+  if (dtype == BST_F64) return dispatch_tb_f64(c, x, xs, y, ys, k, m_lo, m_hi, row_lo, row_hi, st);
+  return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+}
+
+std::vector<int> fuse_plan(int nsteps, int kmax) {
+  std::vector<int> ks;
+  if (kmax < 2 || nsteps < 2) {
+    ks.assign(size_t(nsteps > 0 ? nsteps : 0), 1);
+    return ks;
+  }
+  for (int left = nsteps; left > 0;) {
+    const int k = left < kmax ? left : kmax;
+    ks.push_back(k);
+    left -= k;
+  }
+  if ((int(ks.size()) & 1) != (nsteps & 1)) {
+    // split the last launch of two or more sweeps into two launches
+    for (int i = int(ks.size()) - 1; i >= 0; --i)
+      if (ks[i] >= 2) {
+        const int k = ks[i];
+        ks[i] = k - 1;
+        ks.insert(ks.begin() + i + 1, 1);
+        break;
+      }
+  }
+  return ks;
 }
 
 static void contiguous_strides(int ndim, const int64_t* shape, int64_t* st) {
@@ -367,41 +405,11 @@ int bst_stencil_sweeps(const bst_program* prog, int32_t dtype, int32_t ndim, con
   // Fuse up to kmax sweeps per launch (temporal blocking) where a kernel exists; keep the
   // number of launches of the same parity as nsteps so the result lands in the buffer the
   // contract names.
-  const int kmax = dtype == BST_F32 ? tb_max_f32(c, a, s, b, s) : tb_max_f64(c, a, s, b, s);
-  if (kmax >= 2 && nsteps >= 2) {
-    int left = nsteps;
-    std::vector<int> ks;
-    while (left > 0) {
-      const int k = left < kmax ? left : kmax;
-      ks.push_back(k);
-      left -= k;
-    }
-    if ((int(ks.size()) & 1) != (nsteps & 1)) {
-      // split the last launch of two or more sweeps into two launches
-      for (int i = int(ks.size()) - 1; i >= 0; --i)
-        if (ks[i] >= 2) {
-          const int k = ks[i];
-          ks[i] = k - 1;
-          ks.insert(ks.begin() + i + 1, 1);
-          break;
-        }
-    }
-    void* src = a;
-    void* dst = b;
-    for (int k : ks) {
-      if (k == 1) rc = launch_sweep(c, dtype, src, s, dst, s, 0, c.no[0], static_cast<cudaStream_t>(stream));
-      else
-        rc = dtype == BST_F32 ? dispatch_tb_f32(c, src, s, dst, s, k, static_cast<cudaStream_t>(stream))
-                              : dispatch_tb_f64(c, src, s, dst, s, k, static_cast<cudaStream_t>(stream));
-      if (rc) return rc;
-      std::swap(src, dst);
-    }
-    return BST_OK;
-  }
+  const int kmax = tb_max_sweeps(c, dtype, a, s, b, s);
   void* src = a;
   void* dst = b;
-  for (int i = 0; i < nsteps; ++i) {
-    rc = launch_sweep(c, dtype, src, s, dst, s, 0, c.no[0], static_cast<cudaStream_t>(stream));
+  for (int k : fuse_plan(nsteps, kmax)) {
+    rc = launch_fused(c, dtype, src, s, dst, s, k, 0, c.no[0], 0, c.no[0], static_cast<cudaStream_t>(stream));
     if (rc) return rc;
     std::swap(src, dst);
   }

@@ -12,8 +12,8 @@ int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, cons
   return tb_max_sweeps<double>(r);
 }
 int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
-                    cudaStream_t st) {
-  LaunchReq r{&c, x, {xs[0], xs[1], xs[2]}, y, {ys[0], ys[1], ys[2]}, 0, c.no[0], st};
+                    int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st) {
+  LaunchReq r{&c, x, {xs[0], xs[1], xs[2]}, y, {ys[0], ys[1], ys[2]}, m_lo, m_hi, st, row_lo, row_hi};
   return dispatch_tb<double>(r, k);
 }
 }  // namespace bst

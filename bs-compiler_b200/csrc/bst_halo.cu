@@ -8,6 +8,7 @@
 #include <dlfcn.h>
 #include <nccl.h>  // types and enums only; every call goes through the dlopen'd table
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <mutex>
@@ -249,54 +250,102 @@ int bst_halo_exchange(bst_comm* c, void* slab, int32_t dtype, int64_t plane_elem
   return halo_enqueue(c, slab, dtype, plane_elems, n_local, ghost, static_cast<cudaStream_t>(stream));
 }
 
-int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
-                    void* a, void* b, int32_t nsteps, void* stream) {
+// Canonical form of a slab program: axis 0 widened by `ghost` planes on each side, output
+// plane o reading input plane o + ghost + dm.
+static int slab_canon(const bst_program* prog, int32_t ndim, const int64_t* local_shape, int32_t ghost, Canon* k,
+                      int64_t s[3], int64_t* plane) {
+  int rc = canonicalize(prog, ndim, local_shape, k);
+  if (rc) return rc;
+  if (k->boundary != BST_BOUNDARY_ZERO) return fail(BST_ERR_INVALID, "slab sweeps need a same-size program");
+  const int64_t nl = local_shape[0];
+  *plane = 1;
+  for (int i = 1; i < ndim; ++i) *plane *= local_shape[i];
+  k->n[0] = nl + 2 * int64_t(ghost);
+  k->org[0] = ghost;
+  k->no[0] = nl;
+  int64_t st_t[3];
+  int64_t acc = 1;
+  for (int i = ndim - 1; i >= 0; --i) {
+    st_t[i] = acc;
+    acc *= (i == 0 ? nl + 2 * int64_t(ghost) : local_shape[i]);
+  }
+  logical_strides(ndim, st_t, s);
+  return BST_OK;
+}
+
+int bst_slab_ghost_depth(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                         int32_t* ghost_out) {
+  clear_error();
+  if (!prog || !local_shape || !ghost_out) return fail(BST_ERR_INVALID, "null argument");
+  if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+  if (ndim < 2) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
+  Canon k;
+  int64_t s[3], plane = 0;
+  int rc = canonicalize(prog, ndim, local_shape, &k);
+  if (rc) return rc;
+  const int R = k.R[0];
+  // Probe the fused kernel's limit on the widest layout it could use (16-byte aligned buffers).
+  rc = slab_canon(prog, ndim, local_shape, R * 8, &k, s, &plane);
+  if (rc) return rc;
+  const int kmax = R > 0 ? tb_max_sweeps(k, dtype, nullptr, s, nullptr, s) : 1;
+  *ghost_out = R * (kmax > 1 ? kmax : 1);
+  return BST_OK;
+}
+
+int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                         const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps, void* stream) {
   clear_error();
   if (!c || !prog || !local_shape || !a || !b) return fail(BST_ERR_INVALID, "null argument");
   if (a == b) return fail(BST_ERR_INVALID, "ping-pong slabs must differ");
   if (nsteps < 0) return fail(BST_ERR_INVALID, "negative step count");
+  if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
   if (ndim < 2) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
-  // Canonicalise against the owned extent, then widen axis 0 by the ghost planes.
+  if (ghost < 0 || ghost > (1 << 20)) return fail(BST_ERR_INVALID, "ghost depth out of range");
   Canon k;
-  int rc = canonicalize(prog, ndim, local_shape, &k);
+  int64_t s[3], plane = 0;
+  int rc = slab_canon(prog, ndim, local_shape, ghost, &k, s, &plane);
   if (rc) return rc;
-  if (k.boundary != BST_BOUNDARY_ZERO) return fail(BST_ERR_INVALID, "slab sweeps need a same-size program");
   const int R = k.R[0];
   const int64_t nl = local_shape[0];
-  if (R > 0 && nl < R) return fail(BST_ERR_INVALID, "each rank must own at least `radius` planes");
-  int64_t plane = 1;
-  for (int i = 1; i < ndim; ++i) plane *= local_shape[i];
-  const size_t es = dtype == BST_F64 ? 8 : 4;
-  k.n[0] = nl + 2 * R;  // input includes the ghost planes
-  k.org[0] = R;         // output plane o reads input plane o + R + dm
-  k.no[0] = nl;
-  int64_t st_t[3], s[3];
-  {
-    int64_t acc = 1;
-    for (int i = ndim - 1; i >= 0; --i) {
-      st_t[i] = acc;
-      acc *= (i == 0 ? nl + 2 * R : local_shape[i]);
-    }
+  if (ghost < R) return fail(BST_ERR_INVALID, "ghost depth is below the program's axis-0 radius");
+  // Sweeps fused per exchange: bounded by the kernel and by the ghost depth (k*R planes).
+  int kmax = 1;
+  if (R > 0 && ghost >= 2 * R) {
+    const int kt = tb_max_sweeps(k, dtype, a, s, b, s);
+    kmax = kt < ghost / R ? kt : ghost / R;
   }
-  logical_strides(ndim, st_t, s);
+  const std::vector<int> plan = fuse_plan(nsteps, kmax);
+  int kbig = 1;
+  for (int kk : plan) kbig = kk > kbig ? kk : kbig;
+  const int64_t gx = int64_t(kbig) * R;  // planes exchanged per launch: the deepest read
+  if (c->nranks > 1 && nl < gx) return fail(BST_ERR_INVALID, "each rank must own at least (fused sweeps x radius) planes");
+  const size_t es = dtype == BST_F64 ? 8 : 4;
+  // Intermediate levels are real data everywhere except beyond the global ends.
+  const int64_t big = int64_t(1) << 40;
+  const int64_t row_lo = c->rank == 0 ? 0 : -big;
+  const int64_t row_hi = c->rank == c->nranks - 1 ? nl : big;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   BST_CUDA(cudaSetDevice(c->device));
   char* src = static_cast<char*>(a);
   char* dst = static_cast<char*>(b);
-  const size_t ghost_bytes = size_t(R) * plane * es;
-  const int64_t lo_end = std::min<int64_t>(R, nl);
-  const int64_t hi_begin = std::max<int64_t>(nl - R, lo_end);
-  for (int step = 0; step < nsteps; ++step) {
-    if (step > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));  // src ghosts have arrived
+  const size_t ghost_bytes = size_t(ghost) * plane * es;
+  // The exchange carries the planes [ghost - gx, ghost) below and above the owned range.
+  const size_t skip_bytes = size_t(ghost - gx) * plane * es;
+  const int64_t lo_end = std::min<int64_t>(gx, nl);
+  const int64_t hi_begin = std::max<int64_t>(nl - gx, lo_end);
+  bool first = true;
+  for (int kk : plan) {
+    if (!first) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));  // src ghosts have arrived
+    first = false;
     void* out = dst + ghost_bytes;
     // Boundary planes first: they feed the exchange.
-    rc = launch_sweep(k, dtype, src, s, out, s, 0, lo_end, st);
-    if (!rc && hi_begin < nl) rc = launch_sweep(k, dtype, src, s, out, s, hi_begin, nl, st);
+    rc = launch_fused(k, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, st);
+    if (!rc && hi_begin < nl) rc = launch_fused(k, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, st);
     if (rc) return rc;
-    if (c->nranks > 1 && R > 0) {
+    if (c->nranks > 1 && gx > 0) {
       BST_CUDA(cudaEventRecord(c->ev_bnd, st));
       BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_bnd, 0));
-      rc = halo_enqueue(c, dst, dtype, plane, nl, R, c->comm_stream);
+      rc = halo_enqueue(c, dst + skip_bytes, dtype, plane, nl, int32_t(gx), c->comm_stream);
       if (rc) return rc;
       BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
     } else {
@@ -304,13 +353,24 @@ int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t
     }
     // Interior planes overlap the exchange.
     if (lo_end < hi_begin) {
-      rc = launch_sweep(k, dtype, src, s, out, s, lo_end, hi_begin, st);
+      rc = launch_fused(k, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
       if (rc) return rc;
     }
     std::swap(src, dst);
   }
-  if (nsteps > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
+  if (!plan.empty()) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
   return BST_OK;
+}
+
+int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                    void* a, void* b, int32_t nsteps, void* stream) {
+  clear_error();
+  if (!prog || !local_shape) return fail(BST_ERR_INVALID, "null argument");
+  if (ndim < 2 || ndim > 3) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
+  Canon k;
+  const int rc = canonicalize(prog, ndim, local_shape, &k);
+  if (rc) return rc;
+  return bst_slab_sweeps_deep(c, prog, dtype, ndim, local_shape, k.R[0], a, b, nsteps, stream);
 }
 
 }  // extern "C"

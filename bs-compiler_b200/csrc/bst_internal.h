@@ -51,6 +51,17 @@ void logical_strides(int ndim, const int64_t* strides, int64_t out[3]);
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
                  const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st);
 
+// Temporal blocking.  tb_max_sweeps: most sweeps one launch can fuse for this request
+// (1 = no fused kernel).  launch_fused: k sweeps of output planes [m_lo, m_hi) in one launch
+// (k == 1 is launch_sweep); intermediate values of planes outside [row_lo, row_hi) (output
+// coordinates) are forced to zero, as a single sweep reads zeros outside the grid.
+int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
+int launch_fused(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
+                 int k, int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
+// Sweeps per launch for nsteps ping-pong sweeps, at most kmax per launch, with a launch
+// count of the same parity as nsteps (so the result lands where a per-sweep ping-pong would).
+std::vector<int> fuse_plan(int nsteps, int kmax);
+
 // Device error word (kernels OR bits into it); allocated once per device.
 unsigned* device_error_word();
 // Reads and clears the calling device's error word (synchronizes the stream).

@@ -19,6 +19,9 @@ struct LaunchReq {
   int64_t ys[3];
   int64_t m_lo, m_hi;
   cudaStream_t st;
+  // Temporally blocked launches: rows (output coordinates) whose intermediate levels are
+  // computed; outside it they are ghost cells.  Default: the grid's own rows.
+  int64_t row_lo = 0, row_hi = -1;
 };
 
 template <typename T, int N>

@@ -56,6 +56,7 @@ struct TbArgs {
   long long n_items;
   unsigned* err;
   int vec_store;
+  int row_lo, row_hi;  // output-coordinate rows whose level values are computed; others are ghosts (0)
 };
 
 // Level windows are circular: a level that has been pushed c times keeps its logical row k
@@ -101,10 +102,12 @@ __device__ __forceinline__ void tb_eval(const T (&w)[2 * C::R + 1][C::VX], const
   ((res[Vs] = eval_shape<typename C::shape, T>(TbFetch<T, C, Vs, PH>{w, seg}, c)), ...);
 }
 
-// Per-item constants of a tile.
+// Per-item constants of a tile (rows in output coordinates, 32-bit).
 struct TbTile {
-  long long L0;      // first input row of the item
-  long long mb, me;  // stored output rows
+  int L0;            // row of the item's first input row
+  int mb, me;        // stored output rows
+  int row_lo, row_hi;  // level values outside [row_lo, row_hi) are ghost cells (0)
+  bool rows_safe;    // every row this item touches lies inside [row_lo, row_hi)
   int cmask;         // bit e: this lane's column e lies inside the grid
   bool edge;         // the warp's columns reach outside the grid
   bool store_lane;   // this lane's columns are stored
@@ -113,11 +116,12 @@ struct TbTile {
 
 // Levels L..K for input row i.  Q0 = (pushes of level 0 so far, this step's included) mod W;
 // window l >= 1 has then been pushed Q0 - 2R times (mod W) when it is read, and this step's
-// row of level l goes to slot (Q0 - 1 - 2R) mod W.
+// row of level l goes to slot (Q0 - 1 - 2R) mod W.  `dst` = the store address of level K's
+// row for this lane.
 template <typename T, class C, int L, int Q0>
 __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], const T* edge_row, int lane,
-                                          const TbTile& t, long long i, const Coefs<T, C::shape::NTERMS>& coef,
-                                          const GridDesc& g, T* __restrict__ out, int vec_store) {
+                                          const TbTile& t, int i, const Coefs<T, C::shape::NTERMS>& coef,
+                                          const GridDesc& g, T* dst, int vec_store) {
   if constexpr (L <= C::K) {
     constexpr int W = 2 * C::R + 1;
     constexpr int PH = L == 1 ? Q0 % W : ((Q0 - 2 * C::R) % W + W) % W;  // pushes of window L-1, mod W
@@ -125,11 +129,11 @@ __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], c
     tb_segment<T, C, L == 1>(seg, win[L - 1][(PH + C::R) % W], edge_row, lane);
     T res[C::VX];
     tb_eval<T, C, PH>(win[L - 1], seg, coef, res, std::make_integer_sequence<int, C::VX>{});
-    const long long row = i - (long long)L * C::R;  // grid row this level computed
+    const int row = i - L * C::R;  // row this level computed
     if constexpr (L < C::K) {
-      // Ghost cells of level L+1 are zero: rows outside the grid (warp-uniform), columns
-      // outside the grid (edge tiles only, warp-uniform branch).
-      if (row < 0 || row >= g.no[0]) {
+      // Ghost cells of level L+1 are zero: rows outside [row_lo, row_hi) (warp-uniform, only
+      // checked in items that reach them) and columns outside the grid (edge tiles only).
+      if (!t.rows_safe && (row < t.row_lo || row >= t.row_hi)) {
 #pragma unroll
         for (int e = 0; e < C::VX; ++e) res[e] = T(0);
       } else if (t.edge) {
@@ -140,10 +144,9 @@ __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], c
       constexpr int SLOT = ((Q0 - 1 - 2 * C::R) % W + W) % W;
 #pragma unroll
       for (int e = 0; e < C::VX; ++e) win[L][SLOT][e] = res[e];
-      tb_levels<T, C, L + 1, Q0>(win, edge_row, lane, t, i, coef, g, out, vec_store);
+      tb_levels<T, C, L + 1, Q0>(win, edge_row, lane, t, i, coef, g, dst, vec_store);
     } else {
       if (row >= t.mb && row < t.me && t.store_lane) {
-        T* dst = out + row * g.so[0] + (long long)t.c0 * g.so[2];
         if (vec_store && t.c0 + C::VX <= g.no[2]) {
           using VT = typename Vec16<T>::type;
           VT q;
@@ -161,32 +164,49 @@ __device__ __forceinline__ void tb_levels(T (&win)[C::K][2 * C::R + 1][C::VX], c
   }
 }
 
-// Step P of a group whose first input row has phase GP = (grp * RB) mod W.
-template <typename T, class C, int GP, int P>
+// Step P of a group whose first input row has phase GP = (grp * RB) mod W.  FIRST: the item's
+// first group (level 0's window still filling); FULL: every step of the group is in range.
+template <typename T, class C, int GP, bool FIRST, bool FULL, int P>
 __device__ __forceinline__ void tb_step(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
                                         const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
-                                        const GridDesc& g, T* __restrict__ out, int vec_store) {
+                                        const GridDesc& g, T* dst_grp, int vec_store) {
   constexpr int W = 2 * C::R + 1;
   const int s = grp * C::RB + P;  // input row relative to L0
-  if (s >= total) return;
+  if constexpr (!FULL) {
+    if (s >= total) return;
+  }
   const int col = C::HXI + lane * C::VX;
   // Leading input row into level 0's window: push number s goes to slot s mod W.
   lds_vec<T, C::VX>(sb[C::B] + P * C::PLANE + col, win[0][(GP + P) % W]);
-  if (s < 2 * C::R) return;  // level 0's window is still filling
+  if constexpr (FIRST) {
+    if (s < 2 * C::R) return;  // level 0's window is still filling
+  }
   // Level 0's centre row (s - R) for the warp-edge x-halo; stage offset is compile-time.
   constexpr int REL = P - C::R;  // relative to this group's first row
   constexpr int SK = REL >= 0 ? REL / C::RB : -((-REL + C::RB - 1) / C::RB);
   constexpr int OFF = REL - SK * C::RB;
   const T* edge_row = sb[C::B + SK] + OFF * C::PLANE + col;
-  tb_levels<T, C, 1, (GP + P + 1) % W>(win, edge_row, lane, t, t.L0 + s, coef, g, out, vec_store);
+  tb_levels<T, C, 1, (GP + P + 1) % W>(win, edge_row, lane, t, t.L0 + s, coef, g, dst_grp + P * g.so[0],
+                                       vec_store);
 }
 
-template <typename T, class C, int GP, int... Ps>
+template <typename T, class C, int GP, bool FIRST, bool FULL, int... Ps>
 __device__ __forceinline__ void tb_group(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
                                          const TbTile& t, int grp, int total, const Coefs<T, C::shape::NTERMS>& coef,
-                                         const GridDesc& g, T* __restrict__ out, int vec_store,
-                                         std::integer_sequence<int, Ps...>) {
-  (tb_step<T, C, GP, Ps>(win, sb, lane, t, grp, total, coef, g, out, vec_store), ...);
+                                         const GridDesc& g, T* dst_grp, int vec_store, std::integer_sequence<int, Ps...>) {
+  (tb_step<T, C, GP, FIRST, FULL, Ps>(win, sb, lane, t, grp, total, coef, g, dst_grp, vec_store), ...);
+}
+
+template <typename T, class C, int GP>
+__device__ __forceinline__ void tb_group_any(T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb, int lane,
+                                             const TbTile& t, int grp, int total,
+                                             const Coefs<T, C::shape::NTERMS>& coef, const GridDesc& g, T* dst_grp,
+                                             int vec_store) {
+  using Seq = std::make_integer_sequence<int, C::RB>;
+  if (grp == 0) tb_group<T, C, GP, true, false>(win, sb, lane, t, grp, total, coef, g, dst_grp, vec_store, Seq{});
+  else if ((grp + 1) * C::RB <= total)
+    tb_group<T, C, GP, false, true>(win, sb, lane, t, grp, total, coef, g, dst_grp, vec_store, Seq{});
+  else tb_group<T, C, GP, false, false>(win, sb, lane, t, grp, total, coef, g, dst_grp, vec_store, Seq{});
 }
 
 // Dispatch the group body on its phase (grp * RB) mod W (compile-time slot arithmetic).
@@ -194,10 +214,8 @@ template <typename T, class C, int... GPs>
 __device__ __forceinline__ void tb_group_phase(int phase, T (&win)[C::K][2 * C::R + 1][C::VX], const T* const* sb,
                                                int lane, const TbTile& t, int grp, int total,
                                                const Coefs<T, C::shape::NTERMS>& coef, const GridDesc& g,
-                                               T* __restrict__ out, int vec_store, std::integer_sequence<int, GPs...>) {
-  ((phase == GPs ? tb_group<T, C, GPs>(win, sb, lane, t, grp, total, coef, g, out, vec_store,
-                                       std::make_integer_sequence<int, C::RB>{})
-                 : void()),
+                                               T* dst_grp, int vec_store, std::integer_sequence<int, GPs...>) {
+  ((phase == GPs ? tb_group_any<T, C, GPs>(win, sb, lane, t, grp, total, coef, g, dst_grp, vec_store) : void()),
    ...);
 }
 
@@ -226,9 +244,13 @@ __global__ void __launch_bounds__(32)
     const int chunk = int(item / a.tiles_x);
     const int x0 = tile_x * C::TXO;
     TbTile t;
-    t.mb = g.m_lo + (long long)chunk * a.chunk;
-    t.me = (t.mb + a.chunk < g.m_hi) ? t.mb + a.chunk : g.m_hi;
-    t.L0 = t.mb - (long long)C::K * C::R;
+    t.mb = int(g.m_lo + (long long)chunk * a.chunk);
+    t.me = (t.mb + a.chunk < g.m_hi) ? t.mb + a.chunk : int(g.m_hi);
+    t.L0 = t.mb - C::K * C::R;
+    t.row_lo = a.row_lo;
+    t.row_hi = a.row_hi;
+    const int total = (t.me - t.mb) + 2 * C::K * C::R;  // input rows of the item
+    t.rows_safe = t.L0 >= t.row_lo && t.L0 + total <= t.row_hi;
     t.c0 = x0 - C::HL * C::VX + lane * C::VX;
     t.cmask = 0;
 #pragma unroll
@@ -236,11 +258,12 @@ __global__ void __launch_bounds__(32)
       if (t.c0 + e >= 0 && t.c0 + e < g.no[2]) t.cmask |= 1 << e;
     t.edge = (x0 - C::HL * C::VX < 0) || (x0 - C::HL * C::VX + 32 * C::VX > g.no[2]);
     t.store_lane = lane >= C::HL && lane < 32 - C::HL && t.c0 < g.no[2];
-    const int total = int(t.me - t.mb) + 2 * C::K * C::R;  // input rows of the item
     const int ngroups = (total + C::RB - 1) / C::RB;
     const int qt = ngroups;
     const int cx = x0 - C::HL * C::VX - C::HXI;
-    const int L0 = int(t.L0);
+    const int L0 = t.L0 + g.org[0];  // input-buffer row of the first input row
+    // Store address of level K's row for step s = 0 (row L0 - K*R), this lane's columns.
+    T* const out0 = out + (long long)(t.L0 - C::K * C::R) * g.so[0] + (long long)t.c0 * g.so[2];
     auto issue = [&](int q) {
       const unsigned slot = (q_base + unsigned(q)) % C::NS;
       mbar_expect_tx(&bars[slot], unsigned(C::PLANE * C::RB * sizeof(T)));
@@ -287,11 +310,11 @@ __global__ void __launch_bounds__(32)
         sb[k] = ring + size_t((q_base + unsigned(q < 0 ? 0 : q)) % C::NS) * C::STAGE;
       }
       constexpr int W = 2 * C::R + 1;
+      T* dst_grp = out0 + (long long)grp * C::RB * g.so[0];
       if constexpr (C::RB % W == 0)  // every group starts at phase 0: one body
-        tb_group<T, C, 0>(win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
-                          std::make_integer_sequence<int, C::RB>{});
+        tb_group_any<T, C, 0>(win, sb, lane, t, grp, total, coef, g, dst_grp, a.vec_store);
       else
-        tb_group_phase<T, C>((grp * C::RB) % W, win, sb, lane, t, grp, total, coef, g, out, a.vec_store,
+        tb_group_phase<T, C>((grp * C::RB) % W, win, sb, lane, t, grp, total, coef, g, dst_grp, a.vec_store,
                              std::make_integer_sequence<int, W>{});
     }
     if (failed) break;

@@ -232,6 +232,21 @@ BST_API int bst_halo_exchange(bst_comm* c, void* slab, int32_t dtype, int64_t pl
 BST_API int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
                     const int64_t* local_shape, void* a, void* b, int32_t nsteps, void* stream);
 
+/* Deep halos.  bst_slab_sweeps_deep is bst_slab_sweeps on slabs with `ghost` planes per side
+ * (ghost >= the axis-0 radius R).  Where a temporally blocked kernel exists for the program
+ * it fuses k <= min(kernel limit, ghost / R) sweeps per launch and exchanges k*R planes once
+ * per k sweeps (boundary planes first, interior overlapped), so a run of n sweeps makes about
+ * n/k exchanges instead of n.  Same result-buffer contract (b when nsteps is odd, a when even)
+ * and the same bits as n single sweeps.  Each rank must own at least k*R planes.
+ * bst_slab_ghost_depth reports the depth that allows the most fusion for this program and
+ * local shape (R when nothing fuses).  Replaces the per-step exchange of
+ * crates/basalto-tree/src/executor.rs:91-119 (one exchange per kernel launch). */
+BST_API int bst_slab_ghost_depth(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                                 int32_t* ghost_out);
+BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                                 const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

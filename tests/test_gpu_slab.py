@@ -25,10 +25,12 @@ def _programs():
     return [(P.heat7_3d(), (37, 20, 64), torch.float32, 4),
             (P.jacobi5_2d(), (70, 256), torch.float32, 5),
             (P.box(3, 1, W.box27_weights()), (19, 16, 64), torch.float64, 3),
-            (P.star_3d(P.LAPLACIAN8_COEFFS), (21, 24, 128), torch.float32, 2)]
+            (P.star_3d(P.LAPLACIAN8_COEFFS), (21, 24, 128), torch.float32, 2),
+            (P.jacobi5_2d(), (64, 128), torch.float64, 7),
+            (P.jacobi5_2d(), (96, 516), torch.float32, 13)]
 
 
-@pytest.mark.parametrize("idx", range(4))
+@pytest.mark.parametrize("idx", range(6))
 def test_single_rank_slab_equals_single_grid(idx):
     from basalto.slab import SlabDomain
     import basalto
@@ -44,6 +46,51 @@ def test_single_rank_slab_equals_single_grid(idx):
     a = x.cuda()
     b = torch.empty_like(a)
     ref_gpu = basalto.sweeps(prog, a, b, steps).cpu().numpy()
+    ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
+    assert np.array_equal(got, ref_gpu)
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("dtype,shape,steps,ghost", [
+    (torch.float32, (70, 256), 7, None),      # default depth 5: plan [5, 1, 1]
+    (torch.float32, (64, 520), 10, None),     # [5, 5]
+    (torch.float64, (50, 128), 8, None),      # depth 3: [3, 3, 1, 1]
+    (torch.float32, (33, 96), 5, 2),          # explicit depth 2: [2, 2, 1]
+    (torch.float32, (9, 64), 6, 4),           # owned planes < 2 x depth: boundary launches only
+])
+def test_single_rank_deep_slab(dtype, shape, steps, ghost):
+    """One rank, deep ghosts: fused sweeps over the slab (row range [0, n) as the global
+    ends) give exactly the single-grid bits, with one boundary/interior triple of launches
+    per fused step."""
+    from basalto import program as P
+    from basalto.slab import SlabDomain, fuse_plan
+    import basalto
+    prog = P.jacobi5_2d()
+    x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(5))
+    dom = SlabDomain(prog, shape, dtype=dtype, device="cuda:0", ghost=ghost)
+    try:
+        G = dom.layout.ghost
+        assert G == (ghost if ghost is not None else (5 if dtype == torch.float32 else 3))
+        dom.load(x)
+        torch.cuda.synchronize()
+        n0 = basalto.launch_count()
+        dom.run(steps)
+        torch.cuda.synchronize()
+        launches = basalto.launch_count() - n0
+        got = dom.owned().cpu().numpy()
+    finally:
+        dom.close()
+    plan = fuse_plan(steps, G)
+    nl = shape[0]
+    per = 0
+    for k in plan:
+        gx = max(plan)
+        lo_end = min(gx, nl)
+        hi_begin = max(nl - gx, lo_end)
+        per += 1 + (hi_begin < nl) + (lo_end < hi_begin)
+    assert launches == per
+    a = x.cuda()
+    ref_gpu = basalto.sweeps(prog, a, torch.empty_like(a), steps).cpu().numpy()
     ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
     assert np.array_equal(got, ref_gpu)
     assert np.array_equal(got, ref)

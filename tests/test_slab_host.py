@@ -130,3 +130,95 @@ def test_sharded_sweeps_equal_single_grid(world, case):
                 p.kill()
     assert ok
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _deep_worker(rank, world, port, case, q):
+    """Deep halos: ghost depth G = k*R, k sweeps per exchange.  Each macro-step evaluates k
+    levels over the whole buffer (zeros beyond it), forces levels outside the GLOBAL domain
+    to zero (as the fused kernel does with its row range), keeps the owned planes and
+    exchanges G planes — the scheme bst_slab_sweeps_deep runs."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shape, terms, steps, k, dtype = case
+        g = np.random.default_rng(7)
+        x = g.standard_normal(shape).astype(dtype)
+        R = max(abs(o[0]) for _, _, taps in terms for o in taps)
+        L = SlabLayout(shape, world, rank, k * R)
+        L.validate()
+        buf = np.zeros(L.buffer_shape, dtype)
+        buf[L.owned] = x[L.start:L.start + L.n_local]
+        _exchange(buf, L)
+        lo_mask = slice(0, L.ghost) if rank == 0 else None
+        hi_mask = slice(L.ghost + L.n_local, None) if rank == world - 1 else None
+        left = steps
+        while left:
+            kk = min(k, left)
+            cur = buf
+            for _ in range(kk):
+                cur = O.eval_program(cur, terms)
+                for m in (lo_mask, hi_mask):
+                    if m is not None:
+                        cur[m] = 0
+            nb = np.zeros_like(buf)
+            nb[L.owned] = cur[L.owned]
+            buf = nb
+            _exchange(buf, L)
+            left -= kk
+        parts = [None] * world
+        dist.all_gather_object(parts, buf[L.owned])
+        if rank == 0:
+            got = np.concatenate(parts, 0)
+            ref = O.sweeps(x, lambda u: O.eval_program(u, terms), steps)
+            q.put(bool(np.array_equal(got, ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+_JACOBI = [("mul", 0.25, [(-1, 0), (1, 0), (0, -1), (0, 1)])]
+
+
+@pytest.mark.parametrize("world,case", [
+    (2, ((20, 16), _JACOBI, 7, 3, np.float32)),
+    (3, ((31, 12), _JACOBI, 11, 5, np.float32)),
+    (3, ((25, 9, 8), _heat_terms(), 5, 2, np.float64)),
+])
+def test_deep_halo_scheme_equals_single_grid(world, case):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_deep_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        ok = q.get(timeout=120)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert ok
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def test_slab_ghost_depth_query():
+    """bst_slab_ghost_depth (host-only): fused depth k*R for the 2-D Jacobi kernel, R where
+    nothing fuses; SlabDomain's default caps it by the smallest rank's owned planes."""
+    from basalto import _abi
+    from basalto import program as P
+    from basalto.slab import slab_ghost_depth
+    assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 1, _abi.BST_F32) == 5
+    assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 8, _abi.BST_F64) == 3
+    assert slab_ghost_depth(P.jacobi5_2d(), (12, 8192), 4, _abi.BST_F32) == 3
+    assert slab_ghost_depth(P.heat7_3d(), (64, 64, 64), 2, _abi.BST_F32) == 1
+    assert slab_ghost_depth(P.star_3d(P.LAPLACIAN8_COEFFS), (64, 64, 64), 2, _abi.BST_F32) == 4
+
+
+def test_fuse_plan_parity():
+    from basalto.slab import fuse_plan
+    for kmax in (1, 2, 3, 5):
+        for n in range(0, 40):
+            ks = fuse_plan(n, kmax)
+            assert sum(ks) == n and len(ks) % 2 == n % 2 and all(1 <= k <= max(kmax, 1) for k in ks)
+    assert fuse_plan(7, 5) == [5, 1, 1] and fuse_plan(10, 5) == [5, 5] and fuse_plan(100, 5) == [5] * 20
