@@ -193,6 +193,8 @@ def _workload(args):
     w = WORKLOADS[args.workload]
     if args.shape:
         w = dataclasses.replace(w, shape=tuple(int(v) for v in args.shape.split("x")))
+    if args.dtype:
+        w = dataclasses.replace(w, dtype={"f32": torch.float32, "f64": torch.float64}[args.dtype])
     return w
 
 
@@ -506,6 +508,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="basalto", choices=["basalto", "reference"])
     ap.add_argument("--workload", default="jacobi5_2d")
+    ap.add_argument("--dtype", choices=["f32", "f64"], default=None,
+                    help="override the workload's dtype (e.g. the 27-point box in fp32)")
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
     ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per CPU-baseline sample")
     ap.add_argument("--e2e-steps", type=int, default=3)

@@ -94,18 +94,32 @@ int run_line(const LaunchReq& r) {
 #ifndef BST_STAR_NSX
 #define BST_STAR_NSX 4
 #endif
+// x-halo source per family (measured): shuffles for radius-1 stars, shared-memory vectors
+// for boxes and the radius-4 star.
+#ifndef BST_2D_HALO_LDS
+#define BST_2D_HALO_LDS 0
+#endif
+#ifndef BST_HEAT_HALO_LDS
+#define BST_HEAT_HALO_LDS 0
+#endif
+#ifndef BST_BOX_HALO_LDS
+#define BST_BOX_HALO_LDS 1
+#endif
+#ifndef BST_STAR_HALO_LDS
+#define BST_STAR_HALO_LDS 1
+#endif
 template <typename T>
 constexpr int kRowCols = 32 * (16 / int(sizeof(T)));
 template <typename T, class S>
-using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, BST_2D_RB, BST_2D_NSX>;
-template <typename T, class S, int TY, int PY, int NSX>
-using Cfg3D = MarchCfg<T, S, kRowCols<T>, TY, PY, 1, NSX>;
+using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, BST_2D_RB, BST_2D_NSX, bool(BST_2D_HALO_LDS)>;
+template <typename T, class S, int TY, int PY, int NSX, bool HALO = false>
+using Cfg3D = MarchCfg<T, S, kRowCols<T>, TY, PY, 1, NSX, HALO>;
 template <typename T, class S>
-using CfgHeat = Cfg3D<T, S, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_NSX>;
+using CfgHeat = Cfg3D<T, S, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_NSX, bool(BST_HEAT_HALO_LDS)>;
 template <typename T, class S>
-using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX>;
+using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HALO_LDS)>;
 template <typename T, class S>
-using CfgStar = Cfg3D<T, S, BST_STAR_TY, BST_STAR_PY, BST_STAR_NSX>;
+using CfgStar = Cfg3D<T, S, BST_STAR_TY, BST_STAR_PY, BST_STAR_NSX, bool(BST_STAR_HALO_LDS)>;
 
 template <typename T>
 int dispatch_sweep(const LaunchReq& r) {
@@ -133,7 +147,8 @@ int dispatch_sweep(const LaunchReq& r) {
   if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, false>>>(r);
   if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, CfgStar<T, StarPair3D<4>>>(r);
   if (shape_matches<WStar7>(c)) return run_march_or_direct<T, CfgHeat<T, WStar7>>(r);
-  if (shape_matches<Box<2, 7, false>>(c)) return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, 4, 1, 2>>(r);
+  if (shape_matches<Box<2, 7, false>>(c))
+    return run_march_or_direct<T, Cfg3D<T, Box<2, 7, false>, 4, 1, 2, bool(BST_BOX_HALO_LDS)>>(r);
   if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, true>>>(r);
   return launch_direct_table<T>(r);
 }

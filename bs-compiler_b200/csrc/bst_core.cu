@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -215,6 +216,16 @@ int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], 
   if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st);
   if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st);
   return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+}
+
+Schedule march_schedule() {
+  static const Schedule s = [] {
+    const char* e = std::getenv("BST_MARCH_SCHEDULE");
+    if (e && std::strcmp(e, "balanced") == 0) return Schedule::kBalanced;
+    if (e && std::strcmp(e, "lockstep") == 0) return Schedule::kLockstep;
+    return Schedule::kItems;
+  }();
+  return s;
 }
 
 int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]) {

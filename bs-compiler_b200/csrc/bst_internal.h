@@ -62,6 +62,11 @@ int launch_fused(const Canon& c, int dtype, const void* x, const int64_t xs[3], 
 // count of the same parity as nsteps (so the result lands where a per-sweep ping-pong would).
 std::vector<int> fuse_plan(int nsteps, int kmax);
 
+// Work schedule of the march kernel (MarchArgs).  BST_MARCH_SCHEDULE = items | lockstep |
+// balanced selects one for tuning runs; the default is the measured best.
+enum class Schedule { kItems, kLockstep, kBalanced };
+Schedule march_schedule();
+
 // Device error word (kernels OR bits into it); allocated once per device.
 unsigned* device_error_word();
 // Reads and clears the calling device's error word (synchronizes the stream).

@@ -6,7 +6,8 @@
 //    mbarrier per stage; TMA's out-of-bounds zero fill supplies the Dirichlet-0 ghost
 //    cells, so the interior and the boundary run the same code.  Taps are read from the
 //    ring at compile-time offsets; the result is stored with coalesced global stores.
-//    Persistent: the grid is sized to the SM count and CTAs stride over work items.
+//    Persistent: the grid is at most the resident CTA count; the work schedule (round-robin
+//    items or contiguous balanced shares) is chosen per launch (MarchArgs).
 //  * line_kernel      : 1-D sweep with 128-bit vector loads/stores and warp shuffles for
 //    the neighbour elements held by adjacent lanes.
 //  * direct_kernel    : any layout/stride (the fallback when TMA's 16-byte rules are not
@@ -142,9 +143,13 @@ constexpr int window_depth() {
 
 // ---------------------------------------------------------------------------------
 // March kernel configuration (compile time).
-template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_>
+// HALO_LDS: a row's x-halo comes as whole neighbouring vectors from shared memory (one
+// ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
+// wide radii, dearer in shared-memory bandwidth.
+template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false>
 struct MarchCfg {
   using shape = S;
+  static constexpr bool HALO_LDS = HALO_LDS_;
   static constexpr int VX = 16 / int(sizeof(T));   // elements per 16-byte vector
   static constexpr int TX = TX_;                   // output columns per tile
   static constexpr int TY = TY_;                   // output rows per tile
@@ -191,13 +196,30 @@ struct MarchCfg {
   }
 };
 
+// Work of one launch: tiles_x * tiles_y tile columns of nm planes each.  Two schedules:
+//  * items (balanced == 0): the columns are cut into chunks of `chunk` planes; item
+//    i = tile + tiles * chunk_index, and CTAs take items round-robin.  CTAs running at the
+//    same time hold adjacent tiles of the same planes, so x/y halo re-reads hit L2.
+//  * balanced (balanced == 1): the work is linearised as w = tile * nm + plane, and CTA b
+//    marches the contiguous range [b*W/G, (b+1)*W/G) as one or more segments.  Every CTA
+//    finishes together and M-halo planes are re-read only at segment starts.
 struct MarchArgs {
   GridDesc g;
-  int tiles_x, tiles_y, chunk, n_chunks;
-  long long n_items;
+  int tiles_x, tiles_y;
+  long long nm;        // planes per tile column
+  long long work;      // items (balanced == 0) or tiles * nm (balanced == 1)
+  long long chunk;     // planes per item (balanced == 0)
+  int balanced;
   unsigned* err;
   int vec_store;  // output rows are 16-byte aligned and contiguous in x
 };
+
+// Balanced contiguous range of CTA b among G CTAs over W units.
+__device__ __forceinline__ void cta_range(long long W, long long b, long long G, long long* w0, long long* w1) {
+  const long long base = W / G, rem = W % G;
+  *w0 = b * base + (b < rem ? b : rem);
+  *w1 = *w0 + base + (b < rem ? 1 : 0);
+}
 
 template <typename T>
 struct Vec16;
@@ -258,6 +280,22 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
   }
 #pragma unroll
   for (int e = 0; e < C::VX; ++e) r.seg[K][C::HX + e] = own[e];
+  if constexpr (C::HALO_LDS) {
+    // x-halo as whole neighbouring 16-byte vectors straight from the tile (it holds HX
+    // loaded columns on each side): one ld.shared.v4 per vector instead of a shuffle and a
+    // predicated edge load per element.
+    constexpr int v_lo = floor_div_c(R.lo, C::VX), v_hi = floor_div_c(R.hi, C::VX);
+#pragma unroll
+    for (int vv = v_lo; vv <= v_hi; ++vv) {
+      if (vv == 0) continue;
+      T nb[C::VX];
+      lds_vec<T, C::VX>(rowp + vv * C::VX, nb);
+#pragma unroll
+      for (int e = 0; e < C::VX; ++e)
+        if (vv * C::VX + e >= R.lo && vv * C::VX + e <= R.hi) r.seg[K][C::HX + vv * C::VX + e] = nb[e];
+    }
+    return;
+  }
 #pragma unroll
   for (int e = R.lo; e < 0; ++e) {
     constexpr int dummy = 0;
@@ -385,14 +423,31 @@ __global__ void __launch_bounds__(C::THREADS)
   bool failed = false;
   MarchRegs<T, C> r;
 
-  for (long long item = blockIdx.x; item < a.n_items; item += gridDim.x) {
-    const int tile_x = int(item % a.tiles_x);
-    const long long rest = item / a.tiles_x;
-    const int tile_y = int(rest % a.tiles_y);
-    const int chunk = int(rest / a.tiles_y);
+  const long long tiles = (long long)a.tiles_x * a.tiles_y;
+  long long w_beg, w_end;
+  if (a.balanced) {
+    cta_range(a.work, blockIdx.x, gridDim.x, &w_beg, &w_end);
+  } else {
+    w_beg = blockIdx.x;
+    w_end = a.work;
+  }
+  for (long long w = w_beg; w < w_end;) {
+    long long tile, mb, me;
+    if (a.balanced) {
+      tile = w / a.nm;
+      const long long seg_end = (tile + 1) * a.nm < w_end ? (tile + 1) * a.nm : w_end;
+      mb = g.m_lo + (w - tile * a.nm);
+      me = g.m_lo + (seg_end - tile * a.nm);
+      w = seg_end;
+    } else {
+      tile = w % tiles;
+      mb = g.m_lo + (w / tiles) * a.chunk;
+      me = mb + a.chunk < g.m_hi ? mb + a.chunk : g.m_hi;
+      w += gridDim.x;
+    }
+    const int tile_x = int(tile % a.tiles_x);
+    const int tile_y = int(tile / a.tiles_x);
     const int x0 = tile_x * C::TX, y0 = tile_y * C::TY;
-    const long long mb = g.m_lo + (long long)chunk * a.chunk;
-    const long long me = (mb + a.chunk < g.m_hi) ? mb + a.chunk : g.m_hi;
     const int ngroups = int((me - mb + C::RB - 1) / C::RB);
     const int qt = ngroups - 1 + C::NEED;  // stages this item loads
 

@@ -216,18 +216,40 @@ int launch_march(const LaunchReq& r) {
   const int occ = occupancy(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
   if (occ <= 0) return fail(BST_ERR_CUDA, "march kernel does not fit on an SM");
   const long long resident = (long long)occ * sm_count();
-  long long nchunks = 1;
-  choose_chunks((long long)a.tiles_x * a.tiles_y, nm, C::RB, 2 * C::RM + 2 * C::RB + 8, resident,
-                &a.chunk, &nchunks);
-  a.n_chunks = int(nchunks);
-  a.n_items = (long long)a.tiles_x * a.tiles_y * nchunks;
+  const long long tiles = (long long)a.tiles_x * a.tiles_y;
+  a.nm = nm;
+  long long grid = 0;
+  switch (march_schedule()) {
+    case Schedule::kBalanced:
+      a.balanced = 1;
+      a.work = tiles * nm;
+      grid = a.work < resident ? a.work : resident;
+      break;
+    case Schedule::kLockstep:
+      if (tiles <= resident) {  // one wave: every tile column in floor(resident / tiles) chunks
+        long long s = resident / tiles;
+        if (s > nm) s = nm;
+        a.chunk = (nm + s - 1) / s;
+        a.work = tiles * ((nm + a.chunk - 1) / a.chunk);
+        grid = a.work;
+        break;
+      }
+      [[fallthrough]];
+    default: {
+      int chunk = 0;
+      long long nchunks = 1;
+      choose_chunks(tiles, nm, C::RB, 2 * C::RM + 2 * C::RB + 8, resident, &chunk, &nchunks);
+      a.chunk = chunk;
+      a.work = tiles * nchunks;
+      grid = a.work < resident ? a.work : resident;
+    }
+  }
   a.err = device_error_word();
   if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
   a.vec_store = (reinterpret_cast<uintptr_t>(r.y) % 16 == 0 && r.ys[2] == 1 && (r.ys[1] * E) % 16 == 0 &&
                  (r.ys[0] * E) % 16 == 0)
                     ? 1
                     : 0;
-  const long long grid = a.n_items < resident ? a.n_items : resident;
   dim3 block(C::THREADS);
   kern<<<unsigned(grid), block, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
                                                   make_coefs<T, C::shape::NTERMS>(c));
