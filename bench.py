@@ -195,6 +195,9 @@ def _workload(args):
         w = dataclasses.replace(w, shape=tuple(int(v) for v in args.shape.split("x")))
     if args.dtype:
         w = dataclasses.replace(w, dtype={"f32": torch.float32, "f64": torch.float64}[args.dtype])
+    if args.contract:  # fused multiply-add folding (the reference GPU kernel's arithmetic)
+        w = dataclasses.replace(w, program=w.program.contracted())
+        os.environ["BASALTO_FP_CONTRACT"] = "1"  # the torch.compile leg compiles the same program
     return w
 
 
@@ -481,6 +484,8 @@ def run_basalto(args):
             "config": {"workload": f"{w.name} {'x'.join(map(str, w.shape))}{' per GPU' if ws > 1 else ''}, "
                                    f"{sweeps} sweeps per step",
                        "parallelism": f"z-slab x{ws}" if ws > 1 else "single GPU",
+                       "arithmetic": "fused multiply-add fold (BST_PROGRAM_CONTRACT)" if w.program.contract
+                       else "separately rounded (bit-identical to eager torch)",
                        "l2": f"inputs larger than L2 (2 x {w.points * es / 2**20:.0f} MiB ping-pong)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -508,6 +513,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="basalto", choices=["basalto", "reference"])
     ap.add_argument("--workload", default="jacobi5_2d")
+    ap.add_argument("--contract", action="store_true",
+                    help="fold multiplied terms with fused multiply-add (BST_PROGRAM_CONTRACT) instead of "
+                         "rounding every operation separately")
     ap.add_argument("--dtype", choices=["f32", "f64"], default=None,
                     help="override the workload's dtype (e.g. the 27-point box in fp32)")
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")

@@ -17,6 +17,7 @@ MAX_TERMS = 2304
 
 BST_OK, BST_ERR_INVALID, BST_ERR_UNSUPPORTED, BST_ERR_CUDA, BST_ERR_NCCL, BST_ERR_TIMEOUT, BST_ERR_NO_DEVICE = range(7)
 BST_F32, BST_F64 = 0, 1
+BST_PROGRAM_CONTRACT = 1  # program flag: fold later multiplied terms with fma
 TERM_SUM, TERM_MUL, TERM_DIV = 0, 1, 2
 BOUNDARY_ZERO, BOUNDARY_VALID = 0, 1
 
@@ -28,7 +29,7 @@ class CProgram(ctypes.Structure):
         ("nterms", c_int32),
         ("init_zero", c_int32),
         ("boundary", c_int32),
-        ("reserved", c_int32),
+        ("flags", c_int32),
         ("out_shape", c_int64 * 3),
         ("tap", (c_int32 * 3) * MAX_TAPS),
         ("term_first", c_int32 * MAX_TERMS),

@@ -13,6 +13,10 @@ device_ptr_x, device_ptr_y, device_ptr_z)`.  The differences are deliberate:
   exact stencil (offsets, coefficients and operation order) from the FX graph and passes it
   to the interceptor as a `program`, so the output equals eager torch bit for bit.
 
+BASALTO_FP_CONTRACT=1 compiles stencils with fused multiply-add folding (the arithmetic of
+the reference's GPU kernel, `StencilProgram.contract`); by default every operation is
+rounded separately, as eager torch does.
+
 Graphs that are not single-input linear stencils (including the reference's matmul /
 attention / softmax branches, compiler.py:10-75) are returned unchanged and run eagerly,
 which is exactly what the reference does for them; set BASALTO_FALLBACK_EAGER=0 to make
@@ -34,6 +38,17 @@ from .fx_extract import Unsupported, extract
 log = logging.getLogger("basalto")
 
 _tls = threading.local()
+
+
+def _fp_contract() -> bool:
+    return os.environ.get("BASALTO_FP_CONTRACT", "0") == "1"
+
+
+def _extract(gm, args):
+    prog, tin = extract(gm, args)
+    if _fp_contract():
+        prog = prog.contracted()
+    return prog, tin
 
 
 def _job_id():
@@ -67,7 +82,7 @@ class StencilCallable:
         key = tuple(x.shape)
         entry = self._programs.get(key)
         if entry is None:  # a dynamic-shape graph called with new sizes
-            prog, _ = extract(self.gm, args)
+            prog, _ = _extract(self.gm, args)
             entry = self._programs[key] = (prog, prog.pack(key))
         return entry
 
@@ -95,7 +110,7 @@ def basalto_backend(gm: torch.fx.GraphModule, example_inputs):
     if not example_inputs:
         return gm
     try:
-        prog, tin = extract(gm, list(example_inputs))
+        prog, tin = _extract(gm, list(example_inputs))
     except Unsupported as e:
         if os.environ.get("BASALTO_FALLBACK_EAGER", "1") == "0":
             raise RuntimeError(f"basalto: graph is not a supported stencil ({e})") from e

@@ -19,6 +19,7 @@ Boundary:
 from __future__ import annotations
 
 import ctypes
+import dataclasses
 from dataclasses import dataclass, field
 from typing import Sequence
 
@@ -41,6 +42,11 @@ class StencilProgram:
     init_zero: bool = False
     boundary: str = "zero"                 # "zero" | "valid"
     shrink: tuple[int, ...] = field(default=())   # valid only: output = input - shrink
+    # Fold every multiplied term after the first as one fused multiply-add,
+    # acc = fma(scale, sum, acc) (C-ABI flag BST_PROGRAM_CONTRACT): the reference GPU
+    # kernel's `acc += x * c` as LLVM's NVPTX backend contracts it.  Off: bit-identical to
+    # eager torch.
+    contract: bool = False
 
     def __post_init__(self):
         if self.ndim not in (1, 2, 3):
@@ -89,6 +95,7 @@ class StencilProgram:
         p.nterms = len(self.terms)
         p.init_zero = 1 if self.init_zero else 0
         p.boundary = _abi.BOUNDARY_ZERO if self.boundary == "zero" else _abi.BOUNDARY_VALID
+        p.flags = _abi.BST_PROGRAM_CONTRACT if self.contract else 0
         if self.boundary == "valid":
             if shape is None:
                 raise ValueError("a valid-region program needs the input shape")
@@ -105,6 +112,10 @@ class StencilProgram:
                     p.tap[k][a] = int(v)
                 k += 1
         return p
+
+    def contracted(self, on: bool = True) -> "StencilProgram":
+        """This program with fused multiply-add folding switched on (or off)."""
+        return dataclasses.replace(self, contract=bool(on))
 
     def pack(self, shape: Sequence[int] | None = None) -> bytes:
         """The program as the raw bytes of a C `bst_program` (for the interceptor)."""

@@ -86,7 +86,7 @@ int run_line(const LaunchReq& r) {
 #define BST_BOX_NSX 3
 #endif
 #ifndef BST_STAR_TY
-#define BST_STAR_TY 16
+#define BST_STAR_TY 8
 #endif
 #ifndef BST_STAR_PY
 #define BST_STAR_PY 2
@@ -121,9 +121,35 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 template <typename T, class S>
 using CfgStar = Cfg3D<T, S, BST_STAR_TY, BST_STAR_PY, BST_STAR_NSX, bool(BST_STAR_HALO_LDS)>;
 
+// Whether BST_PROGRAM_CONTRACT changes this program's arithmetic: some multiplied term after
+// the first (only those fold as fma).
+inline bool contract_applies(const Canon& c) {
+  if (!c.contract) return false;
+  for (int g = 1; g < c.nterms; ++g)
+    if (c.terms[g].op == kMul) return true;
+  return false;
+}
+
+// Contracted programs: the 3-D catalog shapes have fused instantiations; others run the
+// runtime-table kernel, which honours the flag too.
+template <typename T>
+int dispatch_contracted(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  if (c.ndim == 3) {
+    if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, CfgHeat<T, Contracted<Heat3D>>>(r);
+    if (shape_matches<Box<1, 7, false>>(c))
+      return run_march_or_direct<T, CfgBox<T, Contracted<Box<1, 7, false>>>>(r);
+    if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, CfgStar<T, Contracted<StarPair3D<4>>>>(r);
+    if (shape_matches<WStar7>(c)) return run_march_or_direct<T, CfgHeat<T, Contracted<WStar7>>>(r);
+    if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, CfgBox<T, Contracted<Box<1, 7, true>>>>(r);
+  }
+  return launch_direct_table<T>(r);
+}
+
 template <typename T>
 int dispatch_sweep(const LaunchReq& r) {
   const Canon& c = *r.c;
+  if (contract_applies(c)) return dispatch_contracted<T>(r);
   if (c.ndim == 1) {
     if (shape_matches<Mean3Line>(c)) return run_line<T, Mean3Line>(r);
     if (shape_matches<Box<1, 1, false>>(c)) return run_line<T, Box<1, 1, false>>(r);

@@ -143,6 +143,8 @@ int canonicalize(const bst_program* p, int ndim, const int64_t* shape, Canon* c)
   k.ndim = ndim;
   k.boundary = p->boundary;
   k.init_zero = p->init_zero ? 1 : 0;
+  if (p->flags & ~int32_t(BST_PROGRAM_CONTRACT)) return fail(BST_ERR_INVALID, "unknown program flags");
+  k.contract = (p->flags & BST_PROGRAM_CONTRACT) ? 1 : 0;
   k.ntaps = p->ntaps;
   k.nterms = p->nterms;
   k.taps.resize(p->ntaps);

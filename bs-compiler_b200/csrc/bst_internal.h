@@ -30,6 +30,7 @@ struct Canon {
   int ndim = 0;
   int boundary = BST_BOUNDARY_ZERO;
   int init_zero = 0;
+  int contract = 0;  // BST_PROGRAM_CONTRACT
   int ntaps = 0, nterms = 0;
   std::vector<Tap> taps;       // centred offsets (input = output + org + tap)
   std::vector<Term> terms;

@@ -294,23 +294,22 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
       for (int e = 0; e < C::VX; ++e)
         if (vv * C::VX + e >= R.lo && vv * C::VX + e <= R.hi) r.seg[K][C::HX + vv * C::VX + e] = nb[e];
     }
-    return;
-  }
+  } else {
+    // x-halo from neighbouring lanes; the tile's edge lanes read shared memory.
 #pragma unroll
-  for (int e = R.lo; e < 0; ++e) {
-    constexpr int dummy = 0;
-    (void)dummy;
-    const int d = (-e + C::VX - 1) / C::VX;  // lanes to the left holding element e
-    T v = __shfl_up_sync(0xffffffffu, own[e + d * C::VX], d, C::LPR);
-    if (lane_x < d) v = rowp[e];
-    r.seg[K][C::HX + e] = v;
-  }
+    for (int e = R.lo; e < 0; ++e) {
+      const int d = (-e + C::VX - 1) / C::VX;  // lanes to the left holding element e
+      T v = __shfl_up_sync(0xffffffffu, own[e + d * C::VX], d, C::LPR);
+      if (lane_x < d) v = rowp[e];
+      r.seg[K][C::HX + e] = v;
+    }
 #pragma unroll
-  for (int e = C::VX; e <= R.hi; ++e) {
-    const int d = e / C::VX;  // lanes to the right holding element e
-    T v = __shfl_down_sync(0xffffffffu, own[e - d * C::VX], d, C::LPR);
-    if (lane_x >= C::LPR - d) v = rowp[e];
-    r.seg[K][C::HX + e] = v;
+    for (int e = C::VX; e <= R.hi; ++e) {
+      const int d = e / C::VX;  // lanes to the right holding element e
+      T v = __shfl_down_sync(0xffffffffu, own[e - d * C::VX], d, C::LPR);
+      if (lane_x >= C::LPR - d) v = rowp[e];
+      r.seg[K][C::HX + e] = v;
+    }
   }
 }
 

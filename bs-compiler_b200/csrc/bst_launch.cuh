@@ -105,7 +105,7 @@ int launch_direct_table(const LaunchReq& r) {
   const long long cap = (long long)sm_count() * 8;
   if (blocks > cap) blocks = cap;
   direct_table_kernel<T><<<unsigned(blocks), 256, 0, r.st>>>(
-      static_cast<const T*>(r.x), static_cast<T*>(r.y), g, &db->p, TableCoefs<T>{db->scale, c.init_zero});
+      static_cast<const T*>(r.x), static_cast<T*>(r.y), g, &db->p, TableCoefs<T>{db->scale, c.init_zero, c.contract});
   e = cudaGetLastError();
   cudaFreeAsync(d, r.st);
   if (e != cudaSuccess) return cuda_fail(e, "direct_table_kernel launch");

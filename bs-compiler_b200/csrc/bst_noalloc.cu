@@ -36,7 +36,7 @@ constexpr int kNoAllocTableBytes = 32 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_table[kNoAllocTableBytes];
 
 // Packed table layout (byte offsets, all from the array's start):
-//   0                     int32 ntaps, nterms, init_zero, reserved
+//   0                     int32 ntaps, nterms, init_zero, (unused)
 //   16                    int16 tap[ntaps][3]                   (logical M, Y, X offsets)
 //   tf = align4(..)       int16 term_first[nterms], int16 term_count[nterms]
 //   to = tf + 4*nterms    uint8 term_op[nterms]
@@ -249,6 +249,7 @@ extern "C" int bst_stencil_apply_noalloc(const bst_program* prog, int32_t dtype,
   if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
   if (ndim < 1 || ndim > 3) return fail(BST_ERR_INVALID, "only 1-D, 2-D and 3-D grids are supported");
   if (prog->ndim != ndim) return fail(BST_ERR_INVALID, "program ndim does not match the grid");
+  if (prog->flags != 0) return fail(BST_ERR_UNSUPPORTED, "program flags (fused multiply-add) are not supported here");
   int64_t oshape[3] = {0, 0, 0};
   for (int i = 0; i < ndim; ++i) {
     if (shape[i] < 0) return fail(BST_ERR_INVALID, "negative extent");

@@ -7,6 +7,7 @@
 // that expression bit for bit.  Offsets are in logical [M, Y, X] space (see
 // bst_types.cuh: a 2-D [y, x] tap (a, b) is (a, 0, b) here, a 1-D tap (a) is (0, 0, a)).
 #pragma once
+#include <type_traits>
 #include <utility>
 #include "bst_types.cuh"
 
@@ -38,6 +39,18 @@ struct ShapeBase {
   static constexpr int NTAPS = NT;
   static constexpr int NTERMS = NG;
 };
+
+// The same shape evaluated with BST_PROGRAM_CONTRACT: every multiplied term after the first
+// folds as one fused multiply-add, acc = fma(scale, sum, acc).  Plain shapes round every
+// operation separately.
+template <class S>
+struct Contracted : S {
+  static constexpr bool CONTRACT = true;
+};
+template <class S, class = void>
+struct contract_of : std::false_type {};
+template <class S>
+struct contract_of<S, std::void_t<decltype(S::CONTRACT)>> : std::bool_constant<S::CONTRACT> {};
 
 #define BST_SHAPE_RADII(NAME)                               \
   static constexpr int RM = radius_of(NAME::tbl, 0);        \
@@ -159,10 +172,21 @@ __device__ __forceinline__ T eval_term(const F& f, const Coefs<T, S::NTERMS>& c)
   else return s;
 }
 
+// acc + term G: separately rounded, or (contracted shapes, multiplied terms) one fma.
+template <class S, int G, class T, class F>
+__device__ __forceinline__ T fold_term(T acc, const F& f, const Coefs<T, S::NTERMS>& c) {
+  if constexpr (contract_of<S>::value && S::tbl.terms[G].op == kMul) {
+    constexpr int cnt = S::tbl.terms[G].count;
+    return fma_rn(c.scale[G], term_sum<S, G, T>(f, std::make_integer_sequence<int, cnt - 1>{}), acc);
+  } else {
+    return add_rn(acc, eval_term<S, G, T>(f, c));
+  }
+}
+
 template <class S, class T, class F, int... Gs>
 __device__ __forceinline__ T fold_terms(T acc, const F& f, const Coefs<T, S::NTERMS>& c,
                                         std::integer_sequence<int, Gs...>) {
-  ((acc = add_rn(acc, eval_term<S, Gs + 1, T>(f, c))), ...);
+  ((acc = fold_term<S, Gs + 1, T>(acc, f, c)), ...);
   return acc;
 }
 
@@ -182,6 +206,10 @@ __device__ __forceinline__ T eval_table(const F& f, const TableProgram& p, const
     T s = f.at(p.tap[first][0], p.tap[first][1], p.tap[first][2]);
     for (int k = 1; k < p.term_count[g]; ++k)
       s = add_rn(s, f.at(p.tap[first + k][0], p.tap[first + k][1], p.tap[first + k][2]));
+    if (g > 0 && c.contract && p.term_op[g] == kMul) {
+      acc = fma_rn(c.scale[g], s, acc);
+      continue;
+    }
     const T t = apply_op<T>(p.term_op[g], c.scale[g], s);
     if (g == 0) acc = c.init_zero ? add_rn(T(0), t) : t;
     else acc = add_rn(acc, t);

@@ -54,6 +54,7 @@ template <typename T>
 struct TableCoefs {
   const T* scale;
   int init_zero;
+  int contract;  // BST_PROGRAM_CONTRACT
 };
 
 // ---- correctly rounded scalar arithmetic, never contracted into FMA -------------
@@ -63,6 +64,9 @@ __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, 
 __device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
 __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(a, b); }
+// a * b + c with one rounding (used only for BST_PROGRAM_CONTRACT programs).
+__device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
 
 template <typename T>
 __device__ __forceinline__ T apply_op(int op, T scale, T s) {

@@ -67,6 +67,14 @@ typedef enum bst_dtype { BST_F32 = 0, BST_F64 = 1 } bst_dtype;
 #define BST_MAX_TERMS 2304
 enum { BST_TERM_SUM = 0, BST_TERM_MUL = 1, BST_TERM_DIV = 2 };
 enum { BST_BOUNDARY_ZERO = 0, BST_BOUNDARY_VALID = 1 };
+/* BST_PROGRAM_CONTRACT: fold every multiplied term after the first as one fused multiply-add,
+ * acc = fma(scale, sum, acc) — the arithmetic of the reference's GPU kernel, whose
+ * `acc += x * c` (crates/basalto-core/src/ir/stencil_3d.rs:232-294) LLVM's NVPTX backend
+ * contracts into fma.  Without it (default) results are bit-identical to eager torch; with
+ * it they differ from eager torch by rounding only (one rounding per term instead of two)
+ * and are bit-identical to a C fma() restatement.  Not accepted by
+ * bst_stencil_apply_noalloc. */
+enum { BST_PROGRAM_CONTRACT = 1 };
 
 typedef struct bst_program {
   int32_t ndim;       /* 1..3 */
@@ -74,7 +82,7 @@ typedef struct bst_program {
   int32_t nterms;     /* 1..BST_MAX_TERMS */
   int32_t init_zero;  /* 1: fold starts from +0.0 */
   int32_t boundary;   /* BST_BOUNDARY_* */
-  int32_t reserved;
+  int32_t flags;      /* BST_PROGRAM_* bits; 0 = every operation rounded separately */
   int64_t out_shape[3];                 /* VALID only: output extents (shape order) */
   int32_t tap[BST_MAX_TAPS][3];         /* offsets, shape order; unused axes 0 */
   int32_t term_first[BST_MAX_TERMS];

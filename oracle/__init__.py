@@ -46,8 +46,9 @@ def naive_box_f64(x: np.ndarray, radius: int, coeffs) -> np.ndarray:
     return out
 
 
-def program_c(x: np.ndarray, terms, init_zero=False, boundary="zero", shrink=()) -> np.ndarray:
-    """Point-by-point C evaluation of a program (terms = [(op, scale, taps), ...])."""
+def program_c(x: np.ndarray, terms, init_zero=False, boundary="zero", shrink=(), contract=False) -> np.ndarray:
+    """Point-by-point C evaluation of a program (terms = [(op, scale, taps), ...]); with
+    `contract`, later multiplied terms fold as acc = fma(scale, sum, acc)."""
     x = np.ascontiguousarray(x)
     nd = x.ndim
     out_shape = x.shape if boundary == "zero" else tuple(x.shape[a] - shrink[a] for a in range(nd))
@@ -60,5 +61,5 @@ def program_c(x: np.ndarray, terms, init_zero=False, boundary="zero", shrink=())
     fn = c_oracle().oracle_program_f32 if x.dtype == np.float32 else c_oracle().oracle_program_f64
     p = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
     fn(p(x), p(out), nd, _i64(x.shape), 0 if boundary == "zero" else 1, _i64(out_shape), int(bool(init_zero)),
-       len(terms), p(op), p(sc), p(cnt), p(taps))
+       len(terms), p(op), p(sc), p(cnt), p(taps), int(bool(contract)))
     return out

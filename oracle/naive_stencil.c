@@ -12,8 +12,13 @@
  *
  * oracle_program_{f32,f64} evaluate the generic program semantics (a left fold of terms,
  * each an optional scale applied to a left-to-right sum of taps) point by point in the
- * element type.  Build with -ffp-contract=off so no multiply-add is fused.
+ * element type.  Build with -ffp-contract=off so no multiply-add is fused implicitly.
+ * With `contract` set, every later multiplied term is folded as one fused multiply-add,
+ * acc = fma(scale, sum, acc) (C99 fma: one rounding), which is how the reference's GPU
+ * kernel accumulates `acc += x * c` once LLVM's NVPTX backend contracts it
+ * (crates/basalto-core/src/ir/stencil_3d.rs:232-294, flir_builder.rs:118-149).
  */
+#include <math.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -48,10 +53,11 @@ void oracle_naive_box_f64(const double* in, double* out, int ndim, const int64_t
   (void)w;
 }
 
-#define DEFINE_PROGRAM(T, SUFFIX)                                                                   \
+#define DEFINE_PROGRAM(T, SUFFIX, FMA)                                                              \
   void oracle_program_##SUFFIX(const T* in, T* out, int ndim, const int64_t* shape, int boundary,  \
                                const int64_t* out_shape, int init_zero, int nterms, const int* op,  \
-                               const double* scale, const int* count, const int* taps) {            \
+                               const double* scale, const int* count, const int* taps,              \
+                               int contract) {                                                      \
     int64_t n[3] = {1, 1, 1}, no[3] = {1, 1, 1};                                                    \
     for (int a = 0; a < ndim; ++a) {                                                                \
       n[3 - ndim + a] = shape[a];                                                                   \
@@ -76,11 +82,12 @@ void oracle_naive_box_f64(const double* in, double* out, int ndim, const int64_t
             const T c = (T)scale[g];                                                                \
             const T t = op[g] == OP_MUL ? (T)(c * s) : (op[g] == OP_DIV ? (T)(s / c) : s);          \
             if (g == 0) acc = init_zero ? (T)((T)0 + t) : t;                                        \
+            else if (contract && op[g] == OP_MUL) acc = FMA(c, s, acc);                             \
             else acc = (T)(acc + t);                                                                \
           }                                                                                         \
           out[(z * no[1] + y) * no[2] + x] = acc;                                                   \
         }                                                                                           \
   }
 
-DEFINE_PROGRAM(float, f32)
-DEFINE_PROGRAM(double, f64)
+DEFINE_PROGRAM(float, f32, fmaf)
+DEFINE_PROGRAM(double, f64, fma)

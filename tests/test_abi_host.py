@@ -149,6 +149,16 @@ def test_apply_rejects_bad_programs_before_any_device_work():
     lib = _abi.lib()
     assert lib.bst_stencil_apply(ctypes.byref(cp), 5, 3, _abi.i64_array([4, 4, 4]), None, ctypes.c_void_p(1),
                                  None, ctypes.c_void_p(2), None) == _abi.BST_ERR_UNSUPPORTED
+    bad = P.heat7_3d().to_c()
+    bad.flags = 6                                                             # only BST_PROGRAM_CONTRACT exists
+    assert _apply(bad, 3, [4, 4, 4]) == _abi.BST_ERR_INVALID
+    assert b"flags" in lib.bst_last_error()
+    fused = P.heat7_3d().contracted().to_c()
+    assert fused.flags == _abi.BST_PROGRAM_CONTRACT
+    # the allocation-free entry point does not take fused multiply-add programs
+    assert lib.bst_stencil_apply_noalloc(ctypes.byref(fused), 0, 3, _abi.i64_array([4, 4, 4]), None,
+                                         ctypes.c_void_p(16), None, ctypes.c_void_p(32),
+                                         None) == _abi.BST_ERR_UNSUPPORTED
 
 
 def test_interceptor_rejects_like_the_reference():
