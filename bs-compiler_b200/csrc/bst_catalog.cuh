@@ -118,8 +118,29 @@ template <typename T, class S>
 using CfgHeat = Cfg3D<T, S, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_NSX, bool(BST_HEAT_HALO_LDS)>;
 template <typename T, class S>
 using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HALO_LDS)>;
+#ifndef BST_STAR_WINDOW
+#define BST_STAR_WINDOW 1
+#endif
 template <typename T, class S>
-using CfgStar = Cfg3D<T, S, BST_STAR_TY, BST_STAR_PY, BST_STAR_NSX, bool(BST_STAR_HALO_LDS)>;
+using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, 1, BST_STAR_NSX, bool(BST_STAR_HALO_LDS), false,
+                         bool(BST_STAR_WINDOW)>;
+// Boxes in ascending order stream: each input plane is applied to every output it touches as
+// it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
+#ifndef BST_BOXS_TY
+#define BST_BOXS_TY 8
+#endif
+#ifndef BST_BOXS_PY
+#define BST_BOXS_PY 2
+#endif
+#ifndef BST_BOXS_NSX
+#define BST_BOXS_NSX 3
+#endif
+#ifndef BST_BOX_STREAM
+#define BST_BOX_STREAM 1
+#endif
+template <typename T, class S>
+using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, 1, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
+                         bool(BST_BOX_STREAM)>;
 
 // Whether BST_PROGRAM_CONTRACT changes this program's arithmetic: some multiplied term after
 // the first (only those fold as fma).
@@ -138,7 +159,7 @@ int dispatch_contracted(const LaunchReq& r) {
   if (c.ndim == 3) {
     if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, CfgHeat<T, Contracted<Heat3D>>>(r);
     if (shape_matches<Box<1, 7, false>>(c))
-      return run_march_or_direct<T, CfgBox<T, Contracted<Box<1, 7, false>>>>(r);
+      return run_march_or_direct<T, CfgBoxS<T, Contracted<Box<1, 7, false>>>>(r);
     if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, CfgStar<T, Contracted<StarPair3D<4>>>>(r);
     if (shape_matches<WStar7>(c)) return run_march_or_direct<T, CfgHeat<T, Contracted<WStar7>>>(r);
     if (shape_matches<Box<1, 7, true>>(c)) return run_march_or_direct<T, CfgBox<T, Contracted<Box<1, 7, true>>>>(r);
@@ -170,7 +191,7 @@ int dispatch_sweep(const LaunchReq& r) {
   }
   // ndim == 3
   if (shape_matches<Heat3D>(c)) return run_march_or_direct<T, CfgHeat<T, Heat3D>>(r);
-  if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, CfgBox<T, Box<1, 7, false>>>(r);
+  if (shape_matches<Box<1, 7, false>>(c)) return run_march_or_direct<T, CfgBoxS<T, Box<1, 7, false>>>(r);
   if (shape_matches<StarPair3D<4>>(c)) return run_march_or_direct<T, CfgStar<T, StarPair3D<4>>>(r);
   if (shape_matches<WStar7>(c)) return run_march_or_direct<T, CfgHeat<T, WStar7>>(r);
   if (shape_matches<Box<2, 7, false>>(c))

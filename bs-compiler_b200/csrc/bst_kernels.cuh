@@ -110,9 +110,8 @@ constexpr bool window_mode() {
   return true;
 }
 
-template <class S, int PY, int VX>
+template <class S, int PY, int VX, bool W = window_mode<S>()>
 constexpr auto make_segs() {
-  constexpr bool W = window_mode<S>();
   constexpr int NMAX = (2 * S::RM + 1) * (PY + 2 * S::RY);
   SegTable<NMAX> t{};
   t.n = 0;
@@ -141,15 +140,63 @@ constexpr int window_depth() {
   return window_mode<S>() ? w : 0;
 }
 
+// Streaming mode: every term reads a single plane offset dm, the fold visits the offsets in
+// ascending order and starts at -RM (box stencils in slowest-axis-major order).  Input planes
+// then arrive in fold order: when plane p arrives, output p+RM starts its fold with the
+// dm = -RM terms, the outputs in between continue with their middle offsets, and output p-RM
+// completes with dm = +RM.  Each input row is read from shared memory once per step instead
+// of once per plane offset, and the result keeps the exact operation order.
+template <class S>
+constexpr bool stream_mode() {
+  if (S::RM == 0 || window_mode<S>()) return false;
+  int prev = -S::RM;
+  if (S::tbl.taps[S::tbl.terms[0].first].dm != -S::RM) return false;
+  for (int g = 0; g < S::NTERMS; ++g) {
+    const Term t = S::tbl.terms[g];
+    const int dm = S::tbl.taps[t.first].dm;
+    for (int k = 1; k < t.count; ++k)
+      if (S::tbl.taps[t.first + k].dm != dm) return false;
+    if (dm < prev) return false;
+    prev = dm;
+  }
+  return true;
+}
+
+// First term whose plane offset is >= dm (stream mode): offset dm's terms are
+// [group_begin(dm), group_begin(dm + 1)).
+template <class S>
+constexpr int group_begin(int dm) {
+  for (int g = 0; g < S::NTERMS; ++g)
+    if (S::tbl.taps[S::tbl.terms[g].first].dm >= dm) return g;
+  return S::NTERMS;
+}
+
+// Stream mode rows: the lead plane's rows -RY .. PY-1+RY, each with the full x-halo.
+template <class S, int PY, int VX>
+constexpr auto make_stream_segs() {
+  SegTable<PY + 2 * S::RY> t{};
+  t.n = PY + 2 * S::RY;
+  for (int i = 0; i < t.n; ++i) t.r[i] = SegRow{S::RM, i - S::RY, -S::RX, VX - 1 + S::RX};
+  return t;
+}
+
+template <bool STREAM, bool WINDOW, class S, int PY, int VX>
+constexpr auto pick_segs() {
+  if constexpr (STREAM) return make_stream_segs<S, PY, VX>();
+  else return make_segs<S, PY, VX, WINDOW>();
+}
+
 // ---------------------------------------------------------------------------------
 // March kernel configuration (compile time).
 // HALO_LDS: a row's x-halo comes as whole neighbouring vectors from shared memory (one
 // ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
 // wide radii, dearer in shared-memory bandwidth.
-template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false>
+template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false,
+          bool STREAM_ = false, bool WINDOW_ = true>
 struct MarchCfg {
   using shape = S;
   static constexpr bool HALO_LDS = HALO_LDS_;
+  static constexpr bool STREAM = STREAM_ && stream_mode<S>();
   static constexpr int VX = 16 / int(sizeof(T));   // elements per 16-byte vector
   static constexpr int TX = TX_;                   // output columns per tile
   static constexpr int TY = TY_;                   // output rows per tile
@@ -166,20 +213,24 @@ struct MarchCfg {
   static constexpr int PLANE = TXL * TYL;          // elements per plane tile
   static constexpr int STAGE_BYTES = round_up_c(PLANE * RB * int(sizeof(T)), 128);
   static constexpr int STAGE = STAGE_BYTES / int(sizeof(T));
-  static constexpr bool WINDOW = window_mode<S>();
-  static constexpr int WM = window_depth<S>();
+  // Window mode (off-centre plane taps from a register window) where the shape allows it
+  // and the configuration asks for it; otherwise every tap is read from the shared ring.
+  static constexpr bool WINDOW = WINDOW_ && window_mode<S>();
+  static constexpr int WM = WINDOW ? window_depth<S>() : 0;
   // Stages read by group g (input planes g*RB + [0, RB-1+2RM] relative to the item's first
   // loaded plane): the window keeps planes behind the current one in registers, so in window
   // mode group g only reads from plane g*RB + RM on and earlier stages retire early.
   static constexpr int NEED = 1 + (RB - 1 + 2 * RM) / RB;  // stages of group 0 (incl. window fill)
-  static constexpr int FIRST_OFF = (WINDOW ? RM : 0) / RB;  // first stage still read, minus g
+  // First stage still read, minus g: stream mode reads only the lead plane (g*RB + P + 2RM),
+  // window mode the centre plane on, otherwise every plane from g*RB on.
+  static constexpr int FIRST_OFF = (STREAM ? 2 * RM : (WINDOW ? RM : 0)) / RB;
   static constexpr int SPAN = NEED - FIRST_OFF;            // stages one steady-state group reads
   // Ring depth.  A group waits before its barrier and refills after it, so every stage a
   // group waits for must have been issued one group earlier: NS >= NEED + 1 covers group 1
   // (from the initial fill) and every later group (from the previous group's refill).
   static constexpr int NS = NEED + 1 > SPAN + NSX_ ? NEED + 1 : SPAN + NSX_;
   static constexpr int SMEM = NS * STAGE_BYTES + 128;      // + alignment slack
-  static constexpr auto SEGS = make_segs<S, PY, VX>();
+  static constexpr auto SEGS = pick_segs<STREAM, WINDOW, S, PY, VX>();
   static constexpr int NSEG = SEGS.n;
   static constexpr int SEGW = VX + 2 * HX;
   static_assert(TXL <= 256 && TYL <= 256 && RB <= 256, "TMA box extent");
@@ -239,6 +290,7 @@ template <typename T, class C>
 struct MarchRegs {
   T win[2 * C::WM + 1][C::PY][C::VX];
   T seg[C::NSEG > 0 ? C::NSEG : 1][C::SEGW];
+  T acc[C::STREAM ? 2 * C::RM + 1 : 1][C::PY][C::VX];  // stream mode: outputs g .. g+2RM in flight
 };
 
 template <typename T, class C, int J, int V>
@@ -248,6 +300,10 @@ struct PointFetch {
   __device__ __forceinline__ T get() const {
     if constexpr (C::WINDOW && (dm != 0 || (dy == 0 && dx == 0))) {
       return r.win[C::WM + dm][J][V];
+    } else if constexpr (C::STREAM) {  // every offset reads the current lead plane's rows
+      constexpr int k = C::seg_index(C::RM, J + dy);
+      static_assert(k >= 0, "tap without a row segment");
+      return r.seg[k][C::HX + V + dx];
     } else {
       constexpr int k = C::seg_index(dm, J + dy);
       static_assert(k >= 0, "tap without a row segment");
@@ -359,26 +415,121 @@ __device__ __forceinline__ void load_segments_at(MarchRegs<T, C>& r, const T* co
   (load_segment<T, C, Ks>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
 }
 
+// ---- stream mode -------------------------------------------------------------------
+// Offset DM's terms for point (J, V) of accumulator slot K; START: DM = -RM, the fold begins
+// (term 0, then the zero-start rule, exactly as eval_shape).
+template <typename T, class C, int DM, bool START, int K, int J, int V>
+__device__ __forceinline__ void stream_point(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c) {
+  using S = typename C::shape;
+  constexpr int gb = group_begin<S>(DM), ge = group_begin<S>(DM + 1);
+  const PointFetch<T, C, J, V> f{r};
+  if constexpr (START) {
+    static_assert(gb == 0 && ge >= 1, "the fold starts with offset -RM");
+    T acc = eval_term<S, 0, T>(f, c);
+    if (c.init_zero) acc = add_rn(T(0), acc);
+    r.acc[K][J][V] = fold_range<S, T, 1>(acc, f, c, std::make_integer_sequence<int, ge - 1>{});
+  } else {
+    r.acc[K][J][V] = fold_range<S, T, gb>(r.acc[K][J][V], f, c, std::make_integer_sequence<int, ge - gb>{});
+  }
+}
+
+template <typename T, class C, int DM, bool START, int K, int J, int... Vs>
+__device__ __forceinline__ void stream_row(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+                                           std::integer_sequence<int, Vs...>) {
+  (stream_point<T, C, DM, START, K, J, Vs>(r, c), ...);
+}
+
+template <typename T, class C, int DM, bool START, int K, int... Js>
+__device__ __forceinline__ void stream_slot(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+                                            std::integer_sequence<int, Js...>) {
+  (stream_row<T, C, DM, START, K, Js>(r, c, std::make_integer_sequence<int, C::VX>{}), ...);
+}
+
+// Steady step: the lead plane is offset RM - K of output slot K (slot 2RM starts, slot 0 ends).
+template <typename T, class C, int... Ks>
+__device__ __forceinline__ void stream_apply(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+                                             std::integer_sequence<int, Ks...>) {
+  (stream_slot<T, C, C::RM - Ks, Ks == 2 * C::RM, Ks>(r, c, std::make_integer_sequence<int, C::PY>{}), ...);
+}
+
+// Rows of relative input plane REL into the segment registers.
+template <typename T, class C, int REL, int... Ks>
+__device__ __forceinline__ void stream_rows(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                            std::integer_sequence<int, Ks...>) {
+  (load_segment<T, C, Ks>(r, stage_plane<T, C, REL>(sb) + toff, 0, lane_x), ...);
+}
+
+// Warm-up plane PL (< 2RM) of an item: it is offset PL - RM - K of output slot K <= PL.
+template <typename T, class C, int PL, int... Ks>
+__device__ __forceinline__ void stream_warm(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+                                            std::integer_sequence<int, Ks...>) {
+  (stream_slot<T, C, PL - C::RM - Ks, Ks == PL, Ks>(r, c, std::make_integer_sequence<int, C::PY>{}), ...);
+}
+
+template <typename T, class C, int... PLs>
+__device__ __forceinline__ void stream_fill(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                            const Coefs<T, C::shape::NTERMS>& c, std::integer_sequence<int, PLs...>) {
+  ((stream_rows<T, C, PLs>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{}),
+    stream_warm<T, C, PLs>(r, c, std::make_integer_sequence<int, PLs + 1>{})),
+   ...);
+}
+
+// Store the PY x VX completed points of slot 0 (same rules as eval_store).
+template <typename T, class C, int... Js>
+__device__ __forceinline__ void stream_store(const MarchRegs<T, C>& r, T* __restrict__ dst, long long so1,
+                                             bool interior, int rows_left, int cols_left, long long so2,
+                                             std::integer_sequence<int, Js...>) {
+  using VT = typename Vec16<T>::type;
+  (
+      [&] {
+        T* d = dst + Js * so1;
+        if (interior) {
+          VT q;
+          T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+          for (int v = 0; v < C::VX; ++v) e[v] = r.acc[0][Js][v];
+          *reinterpret_cast<VT*>(d) = q;
+        } else if (Js < rows_left) {
+#pragma unroll
+          for (int v = 0; v < C::VX; ++v)
+            if (v < cols_left) d[v * so2] = r.acc[0][Js][v];
+        }
+      }(),
+      ...);
+}
+
 // One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store, rotate.
 template <typename T, class C, int P>
 __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                            const Coefs<T, C::shape::NTERMS>& coef, T* dst, long long so1,
                                            bool interior, int rows_left, int cols_left, long long so2) {
-  if constexpr (C::WINDOW) {
-    const T* pl = stage_plane<T, C, P + C::RM + C::WM>(sb) + toff;
+  if constexpr (C::STREAM) {
+    stream_rows<T, C, P + 2 * C::RM>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+    stream_apply<T, C>(r, coef, std::make_integer_sequence<int, 2 * C::RM + 1>{});
+    stream_store<T, C>(r, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
 #pragma unroll
-    for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[2 * C::WM][j]);
-  }
-  if constexpr (C::NSEG > 0)
-    load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
-  eval_store<T, C>(r, coef, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
-  if constexpr (C::WINDOW) {
-#pragma unroll
-    for (int k = 0; k < 2 * C::WM; ++k)
+    for (int k = 0; k < 2 * C::RM; ++k)
 #pragma unroll
       for (int j = 0; j < C::PY; ++j)
 #pragma unroll
-        for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
+        for (int e = 0; e < C::VX; ++e) r.acc[k][j][e] = r.acc[k + 1][j][e];
+  } else {
+    if constexpr (C::WINDOW) {
+      const T* pl = stage_plane<T, C, P + C::RM + C::WM>(sb) + toff;
+#pragma unroll
+      for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[2 * C::WM][j]);
+    }
+    if constexpr (C::NSEG > 0)
+      load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+    eval_store<T, C>(r, coef, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
+    if constexpr (C::WINDOW) {
+#pragma unroll
+      for (int k = 0; k < 2 * C::WM; ++k)
+#pragma unroll
+        for (int j = 0; j < C::PY; ++j)
+#pragma unroll
+          for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
+    }
   }
 }
 
@@ -518,6 +669,10 @@ __global__ void __launch_bounds__(C::THREADS)
             for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[k][j]);
           }
         }
+      }
+      if constexpr (C::STREAM) {
+        if (grp == 0)  // planes mb-RM .. mb+RM-1 start outputs mb .. mb+2RM-1
+          stream_fill<T, C>(r, sb, toff, lane_x, coef, std::make_integer_sequence<int, 2 * C::RM>{});
       }
       const long long m_grp = (long long)grp * C::RB;
       const int planes = int(me - mb - m_grp);

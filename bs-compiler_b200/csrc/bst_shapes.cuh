@@ -190,6 +190,14 @@ __device__ __forceinline__ T fold_terms(T acc, const F& f, const Coefs<T, S::NTE
   return acc;
 }
 
+// Terms G0 .. G0 + sizeof(Is) - 1 folded into acc (continuing a fold).
+template <class S, class T, int G0, class F, int... Is>
+__device__ __forceinline__ T fold_range(T acc, const F& f, const Coefs<T, S::NTERMS>& c,
+                                        std::integer_sequence<int, Is...>) {
+  ((acc = fold_term<S, G0 + Is, T>(acc, f, c)), ...);
+  return acc;
+}
+
 template <class S, class T, class F>
 __device__ __forceinline__ T eval_shape(const F& f, const Coefs<T, S::NTERMS>& c) {
   T acc = eval_term<S, 0, T>(f, c);
