@@ -127,7 +127,7 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, 1, BST_STA
 // Boxes in ascending order stream: each input plane is applied to every output it touches as
 // it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
 #ifndef BST_BOXS_TY
-#define BST_BOXS_TY 8
+#define BST_BOXS_TY 16
 #endif
 #ifndef BST_BOXS_PY
 #define BST_BOXS_PY 2

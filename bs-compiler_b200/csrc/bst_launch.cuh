@@ -136,6 +136,20 @@ constexpr CUtensorMapDataType tma_dtype() {
   return sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT64;
 }
 
+// L2 sector promotion of the march kernel's plane loads (BST_TMA_PROMO: 0 none, 1 64 B,
+// 2 128 B, 3 256 B).
+#ifndef BST_TMA_PROMO
+#define BST_TMA_PROMO 3
+#endif
+inline CUtensorMapL2promotion march_l2_promotion() {
+  switch (BST_TMA_PROMO) {
+    case 0: return CU_TENSOR_MAP_L2_PROMOTION_NONE;
+    case 1: return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+    case 2: return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+    default: return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  }
+}
+
 // Whether the request meets TMA's rules for this configuration.
 template <typename T, class C>
 bool march_eligible(const LaunchReq& r) {
@@ -204,7 +218,7 @@ int launch_march(const LaunchReq& r) {
   if (!enc) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   CUresult cr = enc(&map, tma_dtype<T>(), 3, const_cast<void*>(r.x), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    march_l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(cr)) + ")");
 
   auto kern = march_tma_kernel<T, C>;
