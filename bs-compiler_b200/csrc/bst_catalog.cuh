@@ -68,13 +68,13 @@ int run_line(const LaunchReq& r) {
 #define BST_2D_NSX 4
 #endif
 #ifndef BST_HEAT_TY
-#define BST_HEAT_TY 16
+#define BST_HEAT_TY 64
 #endif
 #ifndef BST_HEAT_PY
-#define BST_HEAT_PY 4
+#define BST_HEAT_PY 2
 #endif
 #ifndef BST_HEAT_NSX
-#define BST_HEAT_NSX 3
+#define BST_HEAT_NSX 2
 #endif
 #ifndef BST_BOX_TY
 #define BST_BOX_TY 8
@@ -264,10 +264,16 @@ int launch_tb2d(const LaunchReq& r) {
 template <typename T, class S, int K>
 using CfgTb = TbCfg<T, S, K, BST_TB_RB, BST_TB_NSX>;
 
+// Sweeps fused per launch at most (fp32: 2..5; fp64 keeps 3, the most its x-halo allows).
+#ifndef BST_TB_KMAX_F32
+#define BST_TB_KMAX_F32 5
+#endif
+
 // Largest number of sweeps one temporally blocked launch can fuse for this request (1 = none).
 template <typename T>
 int tb_max_sweeps(const LaunchReq& r) {
-  if (shape_matches<Jacobi2D>(*r.c) && tb_eligible<T, CfgTb<T, Jacobi2D, 2>>(r)) return sizeof(T) == 4 ? 5 : 3;
+  if (shape_matches<Jacobi2D>(*r.c) && tb_eligible<T, CfgTb<T, Jacobi2D, 2>>(r))
+    return sizeof(T) == 4 ? BST_TB_KMAX_F32 : 3;
   return 1;
 }
 
