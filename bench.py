@@ -219,6 +219,25 @@ class CpuReference:
         self.cf = compile_reference(workload.fn)
         self.y = self.cf(self.x)  # compile + one warm sweep
 
+    def rate_for(self, seconds: float, cap: int):
+        """(Gpts/s, seconds, sweeps): consecutive sweeps until `seconds` of host work have run
+        (at most `cap` sweeps).  Shrinking (valid-region) programs restart from the input."""
+        chain = self.w.program.boundary == "zero"
+        y = self.y if chain else self.x
+        n = 0
+        t0 = time.perf_counter()
+        while True:
+            out = self.cf(y)
+            if chain:
+                y = out
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= seconds or n >= cap:
+                break
+        if chain:
+            self.y = y
+        return self.w.points * n / dt / 1e9, dt, n
+
     def rate(self, sweeps: int):
         """(Gpts/s, seconds) over `sweeps` consecutive sweeps."""
         y = self.y
@@ -521,10 +540,10 @@ def run_basalto(args):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        r, dt = CpuReference(w, threads).rate(args.ref_sweeps)
+        r, dt, n = CpuReference(w, threads).rate_for(args.cpu_seconds, cap=max(1, 20 * sweeps))
         cpu = {"value": round(r, 4), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{args.ref_sweeps} of {sweeps} sweeps on the full {'x'.join(map(str, w.shape))} grid, "
-                         f"eager torch via the reference backend's control flow ({dt:.1f} s)"}
+               "sample": f"{n} consecutive sweeps ({dt:.1f} s) on the full {'x'.join(map(str, w.shape))} grid "
+                         f"({sweeps} sweeps per step), eager torch via the reference backend's control flow"}
 
     if comm is not None:
         torch.cuda.synchronize()
@@ -573,7 +592,9 @@ def main():
     ap.add_argument("--dtype", choices=["f32", "f64"], default=None,
                     help="override the workload's dtype (e.g. the 27-point box in fp32)")
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
-    ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per CPU-baseline sample")
+    ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per step of --impl reference")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--host-input", action="store_true", default=True)

@@ -104,22 +104,17 @@ class SlabLayout:
 
 
 def fuse_plan(nsteps: int, kmax: int) -> list[int]:
-    """Sweeps per fused launch for nsteps ping-pong sweeps, as the C library plans them: at
-    most kmax per launch, with a launch count of nsteps' parity (the result then lands in the
-    buffer a per-sweep ping-pong would use)."""
+    """Sweeps per fused launch for nsteps ping-pong sweeps, as the C library plans them: the
+    fewest launches of at most kmax sweeps, one more if their count does not have nsteps'
+    parity (the result then lands in the buffer a per-sweep ping-pong would use), with the
+    sweeps spread evenly over them, larger launches first."""
     if kmax < 2 or nsteps < 2:
         return [1] * max(nsteps, 0)
-    ks = []
-    left = nsteps
-    while left:
-        ks.append(min(kmax, left))
-        left -= ks[-1]
-    if len(ks) % 2 != nsteps % 2:
-        for i in range(len(ks) - 1, -1, -1):
-            if ks[i] >= 2:
-                ks[i:i + 1] = [ks[i] - 1, 1]
-                break
-    return ks
+    launches = -(-nsteps // kmax)
+    if launches % 2 != nsteps % 2:
+        launches += 1
+    base, rem = divmod(nsteps, launches)
+    return [base + (1 if i < rem else 0) for i in range(launches)]
 
 
 def slab_ghost_depth(program: StencilProgram, global_shape, nranks: int, dtype_code: int) -> int:

@@ -127,7 +127,7 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, 1, BST_STA
 // Boxes in ascending order stream: each input plane is applied to every output it touches as
 // it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
 #ifndef BST_BOXS_TY
-#define BST_BOXS_TY 16
+#define BST_BOXS_TY 32
 #endif
 #ifndef BST_BOXS_PY
 #define BST_BOXS_PY 2
@@ -259,14 +259,14 @@ int launch_tb2d(const LaunchReq& r) {
 #define BST_TB_RB 6  // a multiple of the window (2R+1 = 3): one group body, no phase dispatch
 #endif
 #ifndef BST_TB_NSX
-#define BST_TB_NSX 2
+#define BST_TB_NSX 1
 #endif
 template <typename T, class S, int K>
 using CfgTb = TbCfg<T, S, K, BST_TB_RB, BST_TB_NSX>;
 
 // Sweeps fused per launch at most (fp32: 2..5; fp64 keeps 3, the most its x-halo allows).
 #ifndef BST_TB_KMAX_F32
-#define BST_TB_KMAX_F32 5
+#define BST_TB_KMAX_F32 4
 #endif
 
 // Largest number of sweeps one temporally blocked launch can fuse for this request (1 = none).

@@ -250,21 +250,13 @@ std::vector<int> fuse_plan(int nsteps, int kmax) {
     ks.assign(size_t(nsteps > 0 ? nsteps : 0), 1);
     return ks;
   }
-  for (int left = nsteps; left > 0;) {
-    const int k = left < kmax ? left : kmax;
-    ks.push_back(k);
-    left -= k;
-  }
-  if ((int(ks.size()) & 1) != (nsteps & 1)) {
-    // split the last launch of two or more sweeps into two launches
-    for (int i = int(ks.size()) - 1; i >= 0; --i)
-      if (ks[i] >= 2) {
-        const int k = ks[i];
-        ks[i] = k - 1;
-        ks.insert(ks.begin() + i + 1, 1);
-        break;
-      }
-  }
+  // Fewest launches of at most kmax sweeps, one more if their count has the wrong parity;
+  // the sweeps are then spread evenly (larger launches first), so no launch is left with a
+  // single sweep when n >= 2 x launches.
+  int launches = (nsteps + kmax - 1) / kmax;
+  if ((launches & 1) != (nsteps & 1)) ++launches;
+  const int base = nsteps / launches, rem = nsteps % launches;
+  for (int i = 0; i < launches; ++i) ks.push_back(base + (i < rem ? 1 : 0));
   return ks;
 }
 

@@ -52,9 +52,9 @@ def test_single_rank_slab_equals_single_grid(idx):
 
 
 @pytest.mark.parametrize("dtype,shape,steps,ghost", [
-    (torch.float32, (70, 256), 7, None),      # default depth 5: plan [5, 1, 1]
-    (torch.float32, (64, 520), 10, None),     # [5, 5]
-    (torch.float64, (50, 128), 8, None),      # depth 3: [3, 3, 1, 1]
+    (torch.float32, (70, 256), 7, None),      # default depth 4: plan [3, 2, 2]
+    (torch.float32, (64, 520), 10, None),     # [3, 3, 2, 2]
+    (torch.float64, (50, 128), 8, None),      # depth 3: [2, 2, 2, 2]
     (torch.float32, (33, 96), 5, 2),          # explicit depth 2: [2, 2, 1]
     (torch.float32, (9, 64), 6, 4),           # owned planes < 2 x depth: boundary launches only
 ])
@@ -70,7 +70,7 @@ def test_single_rank_deep_slab(dtype, shape, steps, ghost):
     dom = SlabDomain(prog, shape, dtype=dtype, device="cuda:0", ghost=ghost)
     try:
         G = dom.layout.ghost
-        assert G == (ghost if ghost is not None else (5 if dtype == torch.float32 else 3))
+        assert G == (ghost if ghost is not None else (4 if dtype == torch.float32 else 3))
         dom.load(x)
         torch.cuda.synchronize()
         n0 = basalto.launch_count()

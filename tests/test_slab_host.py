@@ -203,12 +203,12 @@ def test_deep_halo_scheme_equals_single_grid(world, case):
 
 
 def test_slab_ghost_depth_query():
-    """bst_slab_ghost_depth (host-only): fused depth k*R for the 2-D Jacobi kernel, R where
+    """bst_slab_ghost_depth (host-only): fused depth k*R for the 2-D Jacobi kernel (k = 4 fp32, 3 fp64), R where
     nothing fuses; SlabDomain's default caps it by the smallest rank's owned planes."""
     from basalto import _abi
     from basalto import program as P
     from basalto.slab import slab_ghost_depth
-    assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 1, _abi.BST_F32) == 5
+    assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 1, _abi.BST_F32) == 4
     assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 8, _abi.BST_F64) == 3
     assert slab_ghost_depth(P.jacobi5_2d(), (12, 8192), 4, _abi.BST_F32) == 3
     assert slab_ghost_depth(P.heat7_3d(), (64, 64, 64), 2, _abi.BST_F32) == 1
@@ -221,4 +221,8 @@ def test_fuse_plan_parity():
         for n in range(0, 40):
             ks = fuse_plan(n, kmax)
             assert sum(ks) == n and len(ks) % 2 == n % 2 and all(1 <= k <= max(kmax, 1) for k in ks)
-    assert fuse_plan(7, 5) == [5, 1, 1] and fuse_plan(10, 5) == [5, 5] and fuse_plan(100, 5) == [5] * 20
+    assert fuse_plan(7, 5) == [3, 2, 2] and fuse_plan(10, 5) == [5, 5] and fuse_plan(100, 5) == [5] * 20
+    assert fuse_plan(100, 4) == [4] * 22 + [3] * 4 and fuse_plan(2, 4) == [1, 1] and fuse_plan(3, 4) == [3]
+    for n in range(4, 60):  # no single-sweep launch once n >= 2 x launches
+        ks = fuse_plan(n, 4)
+        assert min(ks) >= 2 or n < 2 * len(ks)
