@@ -93,6 +93,10 @@ struct bst_comm {
   double timeout_s = 60.0;
   cudaStream_t comm_stream = nullptr;
   cudaEvent_t ev_bnd = nullptr, ev_comm = nullptr;
+  // Deep-halo passes: boundary launches on a high-priority stream, concurrent with the
+  // interior launch of the same pass.
+  cudaStream_t bnd_stream = nullptr;
+  cudaEvent_t ev_b[2] = {nullptr, nullptr}, ev_int = nullptr;
 };
 
 namespace bst {
@@ -108,10 +112,24 @@ static int wait_comm(bst_comm* c, const char* what) {
     if (st != ncclInProgress) return nccl_fail(st, what);
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (el > c->timeout_s) return fail(BST_ERR_TIMEOUT, std::string(what) + ": timed out");
-    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    // An enqueue normally completes within microseconds: poll tightly first (a sleep costs
+    // ~100 us of scheduler latency per exchange), then back off so a stuck peer does not
+    // burn a core until the timeout.
+    if (el < 2e-3) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
 }  // namespace bst
+
+static void release_cuda(bst_comm* c) {
+  if (c->ev_bnd) cudaEventDestroy(c->ev_bnd);
+  if (c->ev_comm) cudaEventDestroy(c->ev_comm);
+  for (cudaEvent_t& ev : c->ev_b)
+    if (ev) cudaEventDestroy(ev);
+  if (c->ev_int) cudaEventDestroy(c->ev_int);
+  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
+  if (c->bnd_stream) cudaStreamDestroy(c->bnd_stream);
+}
 
 extern "C" {
 
@@ -160,8 +178,14 @@ int bst_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, int32_t
   cudaError_t e = cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_bnd, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_comm, cudaEventDisableTiming);
+  int prio_least = 0, prio_greatest = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetStreamPriorityRange(&prio_least, &prio_greatest);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&c->bnd_stream, cudaStreamNonBlocking, prio_greatest);
+  for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&c->ev_b[i], cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_int, cudaEventDisableTiming);
   if (e != cudaSuccess) {
     nccl().CommAbort(c->comm);
+    release_cuda(c);
     delete c;
     return cuda_fail(e, "comm stream/events");
   }
@@ -169,11 +193,6 @@ int bst_comm_create(const uint8_t id[128], int32_t nranks, int32_t rank, int32_t
   return BST_OK;
 }
 
-static void release_cuda(bst_comm* c) {
-  if (c->ev_bnd) cudaEventDestroy(c->ev_bnd);
-  if (c->ev_comm) cudaEventDestroy(c->ev_comm);
-  if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
-}
 
 int bst_comm_destroy(bst_comm* c) {
   clear_error();
@@ -182,6 +201,7 @@ int bst_comm_destroy(bst_comm* c) {
   if (c->comm) {
     cudaSetDevice(c->device);
     if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
+    if (c->bnd_stream) cudaStreamSynchronize(c->bnd_stream);
     if (nccl().CommFinalize) {
       ncclResult_t r = nccl().CommFinalize(c->comm);
       if (r == ncclSuccess || r == ncclInProgress) rc = wait_comm(c, "ncclCommFinalize");
@@ -301,17 +321,17 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
   if (ndim < 2) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
   if (ghost < 0 || ghost > (1 << 20)) return fail(BST_ERR_INVALID, "ghost depth out of range");
-  Canon k;
+  Canon k_canon;
   int64_t s[3], plane = 0;
-  int rc = slab_canon(prog, ndim, local_shape, ghost, &k, s, &plane);
+  int rc = slab_canon(prog, ndim, local_shape, ghost, &k_canon, s, &plane);
   if (rc) return rc;
-  const int R = k.R[0];
+  const int R = k_canon.R[0];
   const int64_t nl = local_shape[0];
   if (ghost < R) return fail(BST_ERR_INVALID, "ghost depth is below the program's axis-0 radius");
   // Sweeps fused per exchange: bounded by the kernel and by the ghost depth (k*R planes).
   int kmax = 1;
   if (R > 0 && ghost >= 2 * R) {
-    const int kt = tb_max_sweeps(k, dtype, a, s, b, s);
+    const int kt = tb_max_sweeps(k_canon, dtype, a, s, b, s);
     kmax = kt < ghost / R ? kt : ghost / R;
   }
   const std::vector<int> plan = fuse_plan(nsteps, kmax);
@@ -333,32 +353,43 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   const size_t skip_bytes = size_t(ghost - gx) * plane * es;
   const int64_t lo_end = std::min<int64_t>(gx, nl);
   const int64_t hi_begin = std::max<int64_t>(nl - gx, lo_end);
-  bool first = true;
+  // Per pass k (src -> dst): the boundary rows run on the high-priority boundary stream,
+  // concurrently with the interior rows on `st`; both read src and write disjoint rows of dst.
+  //   boundary k  waits for interior k-1 (ev_int) and exchange k-1 (ev_comm: src's ghosts);
+  //   exchange k  (comm stream) waits for boundary k;
+  //   interior k  waits for boundary k-1 (ev_b[(k-1) % 2]; its rows are inside what interior k reads).
+  // Events are waited on before they are re-recorded, so every wait sees the intended pass.
+  const bool exchange = c->nranks > 1 && gx > 0;
+  BST_CUDA(cudaEventRecord(c->ev_int, st));  // src (with its ghosts) is ready on the caller's stream
+  int k = 0;
   for (int kk : plan) {
-    if (!first) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));  // src ghosts have arrived
-    first = false;
     void* out = dst + ghost_bytes;
-    // Boundary planes first: they feed the exchange.
-    rc = launch_fused(k, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, st);
-    if (!rc && hi_begin < nl) rc = launch_fused(k, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, st);
+    BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
+    if (k > 0 && exchange) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
+    rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
+    if (!rc && hi_begin < nl)
+      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd_stream);
     if (rc) return rc;
-    if (c->nranks > 1 && gx > 0) {
-      BST_CUDA(cudaEventRecord(c->ev_bnd, st));
-      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_bnd, 0));
+    BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+    if (exchange) {
+      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
       rc = halo_enqueue(c, dst + skip_bytes, dtype, plane, nl, int32_t(gx), c->comm_stream);
       if (rc) return rc;
       BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
-    } else {
-      BST_CUDA(cudaEventRecord(c->ev_comm, st));
     }
-    // Interior planes overlap the exchange.
+    if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
     if (lo_end < hi_begin) {
-      rc = launch_fused(k, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
+      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
       if (rc) return rc;
     }
+    BST_CUDA(cudaEventRecord(c->ev_int, st));
     std::swap(src, dst);
+    ++k;
   }
-  if (!plan.empty()) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
+  if (k > 0) {
+    BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
+    if (exchange) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
+  }
   return BST_OK;
 }
 

@@ -177,9 +177,43 @@ struct OccHash {
 };
 int occupancy(const void* fn, int threads, int smem);
 
-// Choose the M-chunk so that equal-size items fill whole waves of resident CTAs.
+// Choose the M-chunk so that equal-size items fill whole waves of resident CTAs.  The scan
+// covers up to 4096 chunk counts, so results are remembered per request shape (a multi-pass
+// run repeats the same few shapes, and the host must enqueue a pass faster than it runs).
+inline void choose_chunks_scan(long long base_tiles, long long nm, int rb, int overhead, long long resident,
+                               int* chunk_out, long long* nchunks_out);
 inline void choose_chunks(long long base_tiles, long long nm, int rb, int overhead, long long resident,
                           int* chunk_out, long long* nchunks_out) {
+  struct Key {
+    long long t, m, res;
+    int rb, ov;
+    bool operator==(const Key& o) const { return t == o.t && m == o.m && res == o.res && rb == o.rb && ov == o.ov; }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<long long>()(k.t * 1000003LL ^ k.m * 7919LL ^ k.res) ^ (size_t(k.rb) << 20) ^ size_t(k.ov);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, std::pair<int, long long>, KeyHash> memo;
+  const Key key{base_tiles, nm, resident, rb, overhead};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) {
+      *chunk_out = it->second.first;
+      *nchunks_out = it->second.second;
+      return;
+    }
+  }
+  choose_chunks_scan(base_tiles, nm, rb, overhead, resident, chunk_out, nchunks_out);
+  std::lock_guard<std::mutex> lk(mu);
+  if (memo.size() > 4096) memo.clear();
+  memo.emplace(key, std::make_pair(*chunk_out, *nchunks_out));
+}
+
+inline void choose_chunks_scan(long long base_tiles, long long nm, int rb, int overhead, long long resident,
+                               int* chunk_out, long long* nchunks_out) {
   double best = 1e300;
   int best_chunk = int(nm);
   long long best_n = 1;
