@@ -2,8 +2,8 @@
 
 * one rank (an NCCL communicator of size 1): the boundary/interior split and the slab
   addressing must give exactly the single-grid result;
-* two ranks on two GPUs (skipped with fewer): ghost exchange over NCCL, gathered result equal
-  to the single-grid oracle.  NVLS is off; ranks exchange the NCCL id over gloo; every wait
+* two and four ranks on as many GPUs (skipped with fewer): ghost exchange over NCCL,
+  gathered result equal to the single-grid oracle.  NVLS is off; ranks exchange the NCCL id over gloo; every wait
   is bounded by process-group and join timeouts.
 """
 import os
@@ -134,13 +134,16 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_nccl_exchange_equals_single_grid():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks_nccl_exchange_equals_single_grid(world):
+    """2 ranks: both global ends; 4 ranks: middle ranks with two neighbours as well."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
