@@ -10,16 +10,24 @@ deep ghosts: every fused pass of k sweeps exchanges k ghost rows with each neigh
 NCCL, overlapped with the interior.
 
 value      grid-point updates per second of the whole job (Gpts/s), inputs resident in HBM,
-           CUDA events on the compute stream, max over ranks.
-e2e        the same metric through the public plugin path: pinned host grid -> H2D ->
-           torch.compile(jacobi, backend="basalto") called once per sweep -> D2H, all inside
-           the timed region (N = 1; at N > 1 the slab API, bst_halo_exchange +
-           bst_slab_sweeps_deep, with each rank's slab copied in and out).
-roofline   the Jacobi kernel: algorithmic bytes (8 B per point: one read + one write) per
-           pass over the grid / average pass time, against the measured HBM copy bandwidth.
+           CUDA events on the compute stream, max over ranks.  Inputs smaller than L2 are
+           timed step by step with a 256 MiB write between steps.
+e2e        the same metric through the public API with host buffers: every step copies the
+           grid from pinned host memory, runs basalto.sweeps (C ABI bst_stencil_sweeps) and
+           copies the result back, two steps in flight on separate copy streams.  At N > 1:
+           bst_halo_exchange + bst_slab_sweeps_deep per rank with each slab copied in and out.
+           e2e.torch_compile_per_sweep: torch.compile(fn, backend="basalto") called once per
+           sweep (the drop-in plugin path).
+roofline   the dominant kernel: algorithmic bytes (2 x element size per point: one read + one
+           write) per pass over the grid / average pass time, against the measured HBM copy
+           bandwidth; a temporally blocked pass performs several sweeps for those bytes.
+halo       (N > 1) ghost planes, bytes and time of one exchange timed alone.
+energy     NVML total-energy counter over the timed region, summed over ranks.
 cpu_baseline / --impl reference
            the reference's CPU path: eager torch through the reference backend's control
-           flow (oracle/reference_path.py), all host threads, a bounded number of sweeps.
+           flow (oracle/reference_path.py), all host threads, ~10 s of sweeps.
+--contract fused multiply-add arithmetic (BST_PROGRAM_CONTRACT); --dtype / --shape override
+           the workload's element type / grid.
 """
 from __future__ import annotations
 
