@@ -92,7 +92,7 @@ int run_line(const LaunchReq& r) {
 #define BST_STAR_PY 2
 #endif
 #ifndef BST_STAR_NSX
-#define BST_STAR_NSX 4
+#define BST_STAR_NSX 3
 #endif
 // x-halo source per family (measured): shuffles for radius-1 stars, shared-memory vectors
 // for boxes and the radius-4 star.
@@ -122,7 +122,7 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 #define BST_STAR_WINDOW 1
 #endif
 #ifndef BST_STAR_RB
-#define BST_STAR_RB 1
+#define BST_STAR_RB 2  // two planes per stage: half the per-group bookkeeping per plane
 #endif
 template <typename T, class S>
 using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX, bool(BST_STAR_HALO_LDS),
@@ -136,13 +136,16 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_R
 #define BST_BOXS_PY 2
 #endif
 #ifndef BST_BOXS_NSX
-#define BST_BOXS_NSX 3
+#define BST_BOXS_NSX 2
 #endif
 #ifndef BST_BOX_STREAM
 #define BST_BOX_STREAM 1
 #endif
+#ifndef BST_BOXS_RB
+#define BST_BOXS_RB 2
+#endif
 template <typename T, class S>
-using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, 1, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
+using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, BST_BOXS_RB, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
                          bool(BST_BOX_STREAM)>;
 
 // Whether BST_PROGRAM_CONTRACT changes this program's arithmetic: some multiplied term after
