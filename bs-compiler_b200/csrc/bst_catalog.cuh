@@ -114,8 +114,11 @@ template <typename T, class S>
 using Cfg2D = MarchCfg<T, S, kRowCols<T>, 1, 1, BST_2D_RB, BST_2D_NSX, bool(BST_2D_HALO_LDS)>;
 template <typename T, class S, int TY, int PY, int NSX, bool HALO = false>
 using Cfg3D = MarchCfg<T, S, kRowCols<T>, TY, PY, 1, NSX, HALO>;
+#ifndef BST_HEAT_RB
+#define BST_HEAT_RB 1
+#endif
 template <typename T, class S>
-using CfgHeat = Cfg3D<T, S, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_NSX, bool(BST_HEAT_HALO_LDS)>;
+using CfgHeat = MarchCfg<T, S, kRowCols<T>, BST_HEAT_TY, BST_HEAT_PY, BST_HEAT_RB, BST_HEAT_NSX, bool(BST_HEAT_HALO_LDS)>;
 template <typename T, class S>
 using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HALO_LDS)>;
 #ifndef BST_STAR_WINDOW
