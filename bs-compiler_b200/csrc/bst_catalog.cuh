@@ -147,9 +147,12 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_R
 #ifndef BST_BOXS_RB
 #define BST_BOXS_RB 2
 #endif
+#ifndef BST_BOXS_MINB
+#define BST_BOXS_MINB 1
+#endif
 template <typename T, class S>
 using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, BST_BOXS_RB, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
-                         bool(BST_BOX_STREAM)>;
+                         bool(BST_BOX_STREAM), true, BST_BOXS_MINB>;
 
 // Whether BST_PROGRAM_CONTRACT changes this program's arithmetic: some multiplied term after
 // the first (only those fold as fma).

@@ -192,9 +192,10 @@ constexpr auto pick_segs() {
 // ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
 // wide radii, dearer in shared-memory bandwidth.
 template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false,
-          bool STREAM_ = false, bool WINDOW_ = true>
+          bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1>
 struct MarchCfg {
   using shape = S;
+  static constexpr int MINB = MINB_;  // CTAs per SM the register allocation must allow
   static constexpr bool HALO_LDS = HALO_LDS_;
   static constexpr bool STREAM = STREAM_ && stream_mode<S>();
   static constexpr int VX = 16 / int(sizeof(T));   // elements per 16-byte vector
@@ -546,7 +547,7 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
 }
 
 template <typename T, class C>
-__global__ void __launch_bounds__(C::THREADS)
+__global__ void __launch_bounds__(C::THREADS, C::MINB)
     march_tma_kernel(const __grid_constant__ CUtensorMap tmap, T* __restrict__ out,
                      const MarchArgs a, const Coefs<T, C::shape::NTERMS> coef) {
   extern __shared__ unsigned char smem_raw[];
