@@ -148,7 +148,7 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_R
 #define BST_BOXS_RB 2
 #endif
 #ifndef BST_BOXS_MINB
-#define BST_BOXS_MINB 1
+#define BST_BOXS_MINB 2  // 2 CTAs per SM: the fused fold would otherwise take 76 registers
 #endif
 template <typename T, class S>
 using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, BST_BOXS_RB, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
