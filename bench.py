@@ -3,35 +3,50 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl basalto|reference] [--workload NAME]
     torchrun --nproc-per-node N bench.py --gpus N ...       (N > 1: one process per GPU)
 
-Workload (default): 2-D five-point Jacobi, fp32 8192 x 8192 ~U(-1,1) seed 1, Dirichlet-0
-ghost cells, 100 ping-pong sweeps.  One step = the full 100-sweep run.  At N > 1 every rank
-owns an 8192 x 8192 slab of a (8192*N) x 8192 grid split along rows (weak scaling), with
-deep ghosts: every fused pass of k sweeps exchanges k ghost rows with each neighbour over
-NCCL, overlapped with the interior.
+Workload (default): the 25-point 8th-order star (radius 4), fp32 1024 x 1024 x 1024 ~N(0,1)
+seed 4, Dirichlet-0 ghost cells, 10 sweeps.  One step = the 10 sweeps applied to the seeded
+grid, which stays unchanged (sweep 1 reads it, sweeps 2..10 ping-pong two more buffers), so
+every step does the same work and its result can be checked.  The grid is the largest
+single-GPU configuration (1.07 G points, 4 GiB).
+
+N > 1: the grid is split along Z into one slab per GPU.  "strong" workloads (star-25,
+heat-7) split the one global grid; "weak" ones (box-27 768^3, the 2-D Jacobi grid) stack one
+grid per GPU.  Every rank generates the same seeded global grid on its GPU and keeps its slab
+plus ghost planes, so the N-GPU result is the single-grid result point for point.  Per sweep
+the boundary planes are computed first, their ghost planes cross NVLink in one NCCL group on
+a side stream, and the interior planes compute meanwhile (bst_slab_sweeps_deep).
 
 value      grid-point updates per second of the whole job (Gpts/s), inputs resident in HBM,
            CUDA events on the compute stream, max over ranks.  Inputs smaller than L2 are
            timed step by step with a 256 MiB write between steps.
+parity     after the timed steps, sampled output points (global ends, every rank's first and
+           last planes, random points) are recomputed by the CPU oracle from their input
+           neighbourhood and compared bit for bit; summed over ranks.
 e2e        the same metric through the public API with host buffers: every step copies the
-           grid from pinned host memory, runs basalto.sweeps (C ABI bst_stencil_sweeps) and
-           copies the result back, two steps in flight on separate copy streams.  At N > 1:
-           bst_halo_exchange + bst_slab_sweeps_deep per rank with each slab copied in and out.
+           seeded grid in from pinned host memory, runs the sweeps (basalto.apply +
+           basalto.sweeps, the C ABI's bst_stencil_apply + bst_stencil_sweeps; at N > 1
+           bst_halo_exchange + bst_slab_sweeps_deep per rank) and copies the result back, two
+           steps in flight on separate copy streams.
            e2e.torch_compile_per_sweep: torch.compile(fn, backend="basalto") called once per
-           sweep (the drop-in plugin path).
+           sweep (the drop-in plugin path), N = 1.
 roofline   the dominant kernel: algorithmic bytes (2 x element size per point: one read + one
-           write) per pass over the grid / average pass time, against the measured HBM copy
-           bandwidth; a temporally blocked pass performs several sweeps for those bytes.
+           write) per pass over this rank's grid / average pass time, against the measured HBM
+           copy bandwidth; a temporally blocked pass performs several sweeps for those bytes.
+passes     (N > 1) per-pass device times of the boundary launches, the ghost exchange and the
+           interior launch (CUDA events, two extra untimed steps, max over ranks).
 halo       (N > 1) ghost planes, bytes and time of one exchange timed alone.
-energy     NVML total-energy counter over the timed region, summed over ranks.
+energy     NVML total-energy counter over at least one second of steps, summed over ranks.
 cpu_baseline / --impl reference
            the reference's CPU path: eager torch through the reference backend's control
-           flow (oracle/reference_path.py), all host threads, ~10 s of sweeps.
+           flow (oracle/reference_path.py), all host threads, on a bounded Z-slab sample of the
+           seeded grid.  The reference arm loads none of this repository's native libraries.
 --contract fused multiply-add arithmetic (BST_PROGRAM_CONTRACT); --dtype / --shape override
            the workload's element type / grid.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -42,15 +57,17 @@ import time
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
-for _p in (str(REPO), str(REPO / "bs-compiler_b200")):
-    if _p not in sys.path:
-        sys.path.insert(0, _p)
+PKG_DIR = REPO / "bs-compiler_b200" / "basalto"
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "stencil Gpts/s and % of HBM roofline at 1/2/4/8 B200 vs reference CPU path"
 UNIT = "Gpts/s"
 FALLBACK_HBM_GBS = 6650.0
+DEFAULT_WORKLOAD = "star25_3d"
 
 
 def _peaks():
@@ -75,6 +92,72 @@ def _traffic(workload: str, kernel: str):
     except Exception:
         return None
 
+
+# ---- workload definitions ------------------------------------------------------------------
+
+def _workload_table(native: bool):
+    """The workload table.  native: through the `basalto` package (which loads the native
+    library).  Otherwise program.py and workloads.py are loaded as a stand-alone package
+    without the package's __init__, so no native library of this repository is mapped (the
+    reference arm times the reference's CPU path alone)."""
+    if native:
+        if str(PKG_DIR.parent) not in sys.path:
+            sys.path.insert(0, str(PKG_DIR.parent))
+        from basalto.workloads import WORKLOADS
+        return WORKLOADS
+    import importlib
+    import types
+    name = "_basalto_definitions"
+    if name not in sys.modules:
+        pkg = types.ModuleType(name)
+        pkg.__path__ = [str(PKG_DIR)]
+        sys.modules[name] = pkg
+    return importlib.import_module(f"{name}.workloads").WORKLOADS
+
+
+def _workload(args, table):
+    """The named workload, optionally on a different grid / dtype / arithmetic."""
+    import dataclasses
+    w = table[args.workload]
+    if args.shape:
+        w = dataclasses.replace(w, shape=tuple(int(v) for v in args.shape.split("x")))
+    if args.dtype:
+        w = dataclasses.replace(w, dtype={"f32": torch.float32, "f64": torch.float64}[args.dtype])
+    if args.contract:  # fused multiply-add folding (the reference GPU kernel's arithmetic)
+        w = dataclasses.replace(w, program=w.program.contracted())
+        os.environ["BASALTO_FP_CONTRACT"] = "1"  # the torch.compile leg compiles the same program
+    return w
+
+
+def _dtype_name(w):
+    return "f32" if w.dtype == torch.float32 else "f64"
+
+
+def _native_maps():
+    """This repository's native libraries mapped into the process (Linux /proc/self/maps)."""
+    try:
+        lines = Path("/proc/self/maps").read_text().splitlines()
+    except OSError:
+        return []
+    hits = set()
+    for ln in lines:
+        f = ln.split()
+        if f and f[-1].startswith(str(REPO)) and f[-1].endswith(".so"):
+            hits.add(f[-1])
+    return sorted(hits)
+
+
+def cpu_sample_shape(w):
+    """The bounded sample the CPU legs sweep: a Z-slab of at most 64 planes of a 3-D grid, at
+    most 2048 rows of a 2-D grid, the whole 1-D grid."""
+    if len(w.shape) == 3:
+        return (min(w.shape[0], 64),) + tuple(w.shape[1:])
+    if len(w.shape) == 2:
+        return (min(w.shape[0], 2048), w.shape[1])
+    return tuple(w.shape)
+
+
+# ---- device-side helpers ---------------------------------------------------------------------
 
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 50 ms during the timed region."""
@@ -112,7 +195,7 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.t.join(timeout=2)
-        sm, mx, reasons = [], None, set()
+        sm, pw, mx, reasons = [], [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
@@ -121,6 +204,7 @@ class ClockSampler:
             try:
                 sm.append(float(f[1]))
                 mx = float(f[2])
+                pw.append(float(f[3]))
             except ValueError:
                 continue
             for name, v in zip(names, f[5:9]):
@@ -128,11 +212,12 @@ class ClockSampler:
                     reasons.add(name)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_median": statistics.median(pw) if pw else None}
 
 
 class EnergyMeter:
-    """NVML total-energy counter (millijoules since driver load) read around the timed region."""
+    """NVML total-energy counter (millijoules since driver load)."""
 
     def __init__(self, index: int):
         self.nv = None
@@ -210,179 +295,257 @@ def _init_pg(ws, rank, local, backend):
 
     import torch.distributed as dist
     if ws > 1 and not dist.is_initialized():
-        dist.init_process_group(backend, rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group(backend, rank=rank, world_size=ws, timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local) if backend == "nccl" else None)
     return dist
 
 
+# ---- CPU legs ------------------------------------------------------------------------------
+
 class CpuReference:
-    """Eager torch on the host through the reference backend's control flow."""
+    """Eager torch on the host through the reference backend's control flow, on a bounded
+    sample grid of the workload (cpu_sample_shape), every sweep from the seeded sample."""
 
     def __init__(self, workload, threads: int | None = None):
         from oracle.reference_path import compile_reference
         if threads:
             torch.set_num_threads(threads)
         self.w = workload
-        self.x = workload.make_input()  # CPU, the configuration's own seeded grid
+        self.shape = cpu_sample_shape(workload)
+        self.x = workload.make_input(shape=self.shape)  # CPU generator: the configuration's seeded stream
+        self.points = int(np.prod(self.shape))
         self.cf = compile_reference(workload.fn)
-        self.y = self.cf(self.x)  # compile + one warm sweep
+        self.cf(self.x)  # compile + one warm sweep
 
-    def rate_for(self, seconds: float, cap: int):
-        """(Gpts/s, seconds, sweeps): consecutive sweeps until `seconds` of host work have run
-        (at most `cap` sweeps).  Shrinking (valid-region) programs restart from the input."""
-        chain = self.w.program.boundary == "zero"
-        y = self.y if chain else self.x
-        n = 0
+    def sweep(self):
         t0 = time.perf_counter()
-        while True:
-            out = self.cf(y)
-            if chain:
-                y = out
+        self.cf(self.x)
+        return time.perf_counter() - t0
+
+    def rate_for(self, seconds: float):
+        """(Gpts/s, seconds, sweeps): whole sweeps until `seconds` of host work have run."""
+        n, dt = 0, 0.0
+        while dt < seconds:
+            dt += self.sweep()
             n += 1
-            dt = time.perf_counter() - t0
-            if dt >= seconds or n >= cap:
-                break
-        if chain:
-            self.y = y
-        return self.w.points * n / dt / 1e9, dt, n
+        return self.points * n / dt / 1e9, dt, n
 
-    def rate(self, sweeps: int):
-        """(Gpts/s, seconds) over `sweeps` consecutive sweeps."""
-        y = self.y
-        t0 = time.perf_counter()
-        for _ in range(sweeps):
-            y = self.cf(y)
-        dt = time.perf_counter() - t0
-        self.y = y
-        return self.w.points * sweeps / dt / 1e9, dt
-
-
-def _workload(args):
-    """The named workload, optionally on a different grid (--shape, e.g. for profiling)."""
-    import dataclasses
-
-    from basalto.workloads import WORKLOADS
-    w = WORKLOADS[args.workload]
-    if args.shape:
-        w = dataclasses.replace(w, shape=tuple(int(v) for v in args.shape.split("x")))
-    if args.dtype:
-        w = dataclasses.replace(w, dtype={"f32": torch.float32, "f64": torch.float64}[args.dtype])
-    if args.contract:  # fused multiply-add folding (the reference GPU kernel's arithmetic)
-        w = dataclasses.replace(w, program=w.program.contracted())
-        os.environ["BASALTO_FP_CONTRACT"] = "1"  # the torch.compile leg compiles the same program
-    return w
+    def describe(self):
+        return (f"one sweep per step over a {'x'.join(map(str, self.shape))} sample of the "
+                f"{'x'.join(map(str, self.w.shape))} grid (same distribution and seed), eager torch through the "
+                f"reference backend's control flow")
 
 
 def run_reference(args):
     ws, rank, local = _dist()
-    from basalto.workloads import WORKLOADS
-    w = _workload(args)
     if rank != 0:
         return
+    table = _workload_table(native=False)
+    w = _workload(args, table)
     threads = os.cpu_count() or 1
     ref = CpuReference(w, threads)
-    per_step = max(1, args.ref_sweeps)
-    rates = []
+    times = []
     for i in range(args.warmup + args.steps):
-        r, dt = ref.rate(per_step)
+        dt = ref.sweep()
         if i >= args.warmup:
-            rates.append((r, dt))
-    value = statistics.median(r for r, _ in rates)
-    ms = statistics.median(dt for _, dt in rates) * 1e3 / per_step * w.steps
+            times.append(dt)
+    ms = statistics.median(times) * 1e3
+    value = ref.points / (ms * 1e-3) / 1e9
+    loaded = _native_maps()
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32" if w.dtype == torch.float32 else "f64",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"{w.name} {'x'.join(map(str, w.shape))} {w.steps} sweeps",
-                   "sample": f"{per_step} sweep(s) per step on the full grid; ms_per_step scaled to {w.steps} sweeps"},
+        "scaling": w.scaling if w.scaling != "replicas" else "weak", "vs_baseline": None,
+        "dtype": _dtype_name(w), "data": "synthetic", "impl": "reference",
+        "config": {"workload": w.label(), "sample": ref.describe(),
+                   "step": "one sampled sweep (ms_per_step is the time of that sweep)"},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{per_step} of {w.steps} sweeps per step, full {'x'.join(map(str, w.shape))} grid"},
+                         "sample": ref.describe()},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "native_libraries_loaded": loaded,
     }
+    if loaded:
+        raise SystemExit(f"reference arm mapped this repository's native code: {loaded}")
     print(json.dumps(line), flush=True)
 
 
-def run_basalto(args):
-    import ctypes
+# ---- parity: sampled points against the oracle ---------------------------------------------
 
+def sample_points(gshape, owners, seed=11, n_random=4):
+    """Global output points to check: grid corners, every rank's first and last two planes,
+    plus random points.  owners: list of (start, n_local) per rank along axis 0."""
+    g = np.random.default_rng(seed)
+    nd = len(gshape)
+    zs = {0, gshape[0] - 1}
+    for s, n in owners:
+        for z in (s, s + 1, s + n - 2, s + n - 1):
+            if 0 <= z < gshape[0]:
+                zs.add(z)
+    pts = []
+    for i, z in enumerate(sorted(zs)):
+        rest = [int(g.integers(0, e)) if (i % 3) else (0 if i % 2 else e - 1) for e in gshape[1:]]
+        pts.append([z] + rest)
+    for _ in range(n_random):
+        pts.append([int(g.integers(0, e)) for e in gshape])
+    if nd == 3:
+        pts.append([gshape[0] - 1, gshape[1] - 1, 0])
+    return [tuple(p) for p in pts]
+
+
+def oracle_at_point(x_box: np.ndarray, box_lo, gshape, point, prog, sweeps: int):
+    """The program's value after `sweeps` sweeps at global `point`, computed by the oracle from
+    the input box x_box (global origin box_lo) covering point +- sweeps x radius, clipped to
+    the grid.  After every sweep the box loses `radius` cells on each face that is not a grid
+    face (their zero padding is not the real neighbourhood), so what remains is exact."""
+    from oracle import stencil_oracle as O
+    terms = [(t.op, t.scale, t.taps) for t in prog.terms]
+    R = prog.radius()
+    x = x_box
+    lo = list(box_lo)
+    for _ in range(sweeps):
+        x = O.eval_program(x, terms, prog.init_zero, "zero")
+        sl = []
+        for a in range(x.ndim):
+            c0 = R[a] if lo[a] > 0 else 0
+            c1 = R[a] if lo[a] + x.shape[a] < gshape[a] else 0
+            sl.append(slice(c0, x.shape[a] - c1))
+            lo[a] += c0
+        x = x[tuple(sl)]
+    return x[tuple(point[a] - lo[a] for a in range(x.ndim))]
+
+
+def neighbourhood(x_global: torch.Tensor, point, reach):
+    lo = [max(0, p - r) for p, r in zip(point, reach)]
+    hi = [min(e, p + r + 1) for p, r, e in zip(point, reach, x_global.shape)]
+    box = x_global[tuple(slice(a, b) for a, b in zip(lo, hi))].cpu().numpy()
+    return box, lo
+
+
+# ---- the measured arm ----------------------------------------------------------------------
+
+def run_basalto(args):
+    if str(PKG_DIR.parent) not in sys.path:
+        sys.path.insert(0, str(PKG_DIR.parent))
     import basalto
     from basalto import _abi
-    from basalto.workloads import WORKLOADS
+    from basalto.slab import fuse_plan, partition, slab_ghost_depth
 
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = _init_pg(ws, rank, local, "nccl") if ws > 1 else None
-    w = _workload(args)
+    w = _workload(args, _workload_table(native=True))
     prog = w.program
     sweeps = w.steps
     stream = torch.cuda.current_stream(dev)
     es = w.elem_size
+    lib = _abi.lib()
+    dt = _abi.BST_F32 if w.dtype == torch.float32 else _abi.BST_F64
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    sharded = ws > 1 and w.scaling in ("strong", "weak")
+    gshape = w.global_shape(ws) if sharded else tuple(w.shape)
 
-    if ws == 1:
-        a = w.make_input(device=dev)
+    # The seeded global grid, generated on this GPU (every rank generates the same grid).
+    x_global = w.make_input(shape=gshape, device=dev)
+    R = prog.radius()
+    reach = [r * sweeps for r in R]
+
+    comm = None
+    if not sharded:
+        owners = [(0, gshape[0])]
+        my_start, n_local = 0, gshape[0]
+        x0 = x_global
         if prog.boundary == "zero":
-            b = torch.empty_like(a)
+            a = torch.empty_like(x0)
+            b = torch.empty_like(x0)
+
+            def step_on(src, pa, pb):
+                basalto.apply(prog, src, out=pa)
+                return basalto.sweeps(prog, pa, pb, sweeps - 1) if sweeps > 1 else pa
 
             def step():
-                basalto.sweeps(prog, a, b, sweeps)
-        else:  # a shrinking (valid-region) stencil: one sweep per step into its own output
-            b = torch.empty(prog.out_shape(a.shape), dtype=a.dtype, device=dev)
+                return step_on(x0, a, b)
+        else:  # a shrinking (valid-region) stencil: every sweep from the input into its own output
+            b = torch.empty(prog.out_shape(x0.shape), dtype=x0.dtype, device=dev)
 
-            def step():
+            def step_on(src, pa, pb):
                 for _ in range(sweeps):
-                    basalto.apply(prog, a, out=b)
+                    basalto.apply(prog, src, out=pb)
+                return pb
 
-        points_job = w.points
-        comm = None
+            def step():
+                return step_on(x0, None, b)
+        local_points = w.points
+        points_job = w.points * (ws if ws > 1 else 1)  # replicas: every rank runs the whole grid
+        if ws > 1:
+            owners = [(0, gshape[0])]
     else:
-        # Weak scaling: each rank owns a full-size slab; deep ghost planes along axis 0 (the
-        # fused kernel's k x radius, so one exchange per k sweeps).
-        from basalto.slab import fuse_plan, slab_ghost_depth
-        R = prog.radius()[0]
-        local_shape = list(w.shape)
-        dt = _abi.BST_F32 if w.dtype == torch.float32 else _abi.BST_F64
-        G = slab_ghost_depth(prog, [local_shape[0] * ws] + local_shape[1:], ws, dt)
-        g = torch.Generator(device=dev).manual_seed(w.seed + 1000 * rank)
-        a = torch.zeros([local_shape[0] + 2 * G] + local_shape[1:], dtype=w.dtype, device=dev)
-        b = torch.zeros_like(a)
-        a[G:G + local_shape[0]].copy_(torch.rand(local_shape, generator=g, dtype=w.dtype, device=dev) * 2 - 1)
+        owners = [partition(gshape[0], ws, r) for r in range(ws)]
+        my_start, n_local = owners[rank]
+        G = slab_ghost_depth(prog, gshape, ws, dt)
+        local_shape = [n_local] + list(gshape[1:])
+        plane = int(np.prod(gshape[1:]))
+        x0 = torch.zeros([n_local + 2 * G] + list(gshape[1:]), dtype=w.dtype, device=dev)
+        lo, hi = max(0, my_start - G), min(gshape[0], my_start + n_local + G)
+        x0[lo - (my_start - G):hi - (my_start - G)].copy_(x_global[lo:hi])
+        a = torch.zeros_like(x0)
+        b = torch.zeros_like(x0)
         uid = (ctypes.c_uint8 * 128)()
         obj = [None]
         if rank == 0:
-            _abi.check(_abi.lib().bst_nccl_get_unique_id(uid))
+            _abi.check(lib.bst_nccl_get_unique_id(uid))
             obj[0] = bytes(uid)
         dist.broadcast_object_list(obj, src=0)
         uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
         h = ctypes.c_void_p()
-        _abi.check(_abi.lib().bst_comm_create(uid, ws, rank, local, 120.0, ctypes.byref(h)))
+        _abi.check(lib.bst_comm_create(uid, ws, rank, local, 120.0, ctypes.byref(h)))
         comm = h
         cp = prog.to_c(local_shape)
-        plane = 1
-        for s in local_shape[1:]:
-            plane *= s
-        sp = ctypes.c_void_p(stream.cuda_stream)
-        _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0], G, sp))
         shp = _abi.i64_array(local_shape)
 
-        def step():
-            _abi.check(_abi.lib().bst_slab_sweeps_deep(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
-                                                       ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(b.data_ptr()),
-                                                       sweeps, sp))
+        def slab_sweeps(src, dst, n):
+            _abi.check(lib.bst_slab_sweeps_deep(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
+                                                ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
+                                                n, sp))
 
-        # Passes over the slab per step (each pass = boundary launches + interior launch).
-        slab_passes = len(fuse_plan(sweeps, G // R if R else 1))
-        points_job = w.points * ws
+        def step_on(src, pa, pb):
+            slab_sweeps(src, pa, 1)          # sweep 1 reads the seeded slab, which stays unchanged
+            if sweeps > 1:
+                slab_sweeps(pa, pb, sweeps - 1)
+                return pb if (sweeps - 1) % 2 else pa
+            return pa
+
+        def step():
+            return step_on(x0, a, b)
+
+        kmax = max(1, G // R[0]) if R[0] else 1
+        slab_passes = 1 + len(fuse_plan(sweeps - 1, kmax))
+        local_points = n_local * plane
+        points_job = int(np.prod(gshape))
+
+    # Parity sample: the input neighbourhood of every sampled point this rank owns.
+    check = []
+    if prog.boundary == "zero":
+        for p in sample_points(gshape, owners):
+            if my_start <= p[0] < my_start + n_local or not sharded:
+                box, lo_box = neighbourhood(x_global, p, reach)
+                check.append((p, box, lo_box))
+    else:
+        pts = [(0,), (w.out_points - 1,), (w.out_points // 2,)]
+        for p in pts:
+            check.append((p, x_global[p[0]:p[0] + 3].cpu().numpy(), None))
+    if sharded:
+        del x_global
+        torch.cuda.empty_cache()
 
     # ---- timed region (device time, CUDA events on the compute stream) -------------------
     l2_bytes = 126 << 20
     flush = None
-    if w.points * es < l2_bytes:  # the input fits in L2: flush it between timed steps
+    if local_points * es < l2_bytes:  # the input fits in L2: flush it between timed steps
         flush = torch.zeros(256 << 20, dtype=torch.uint8, device=dev)
         l2_note = "L2 flushed before every timed step (256 MiB write, outside the timed windows)"
     else:
-        l2_note = f"inputs larger than L2 (2 x {w.points * es / 2**20:.0f} MiB ping-pong)"
+        l2_note = f"inputs larger than L2 ({local_points * es / 2**20:.0f} MiB grid per GPU, 3 buffers)"
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -390,17 +553,16 @@ def run_basalto(args):
         dist.barrier()
     clocks = ClockSampler(local)
     clocks.start()
-    energy = EnergyMeter(local)
-    mj0 = energy.read()
     n0 = basalto.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    result = None
     if flush is None:  # inputs larger than L2: consecutive steps cannot hit in L2
         e0.record(stream)
         for _ in range(args.steps):
-            step()
+            result = step()
         e1.record(stream)
         torch.cuda.synchronize()
         ms_total = e0.elapsed_time(e1)
@@ -409,20 +571,14 @@ def run_basalto(args):
         for a0, a1 in evs:
             flush.add_(1)  # writes 256 MiB (> L2) between timed steps
             a0.record(stream)
-            step()
+            result = step()
             a1.record(stream)
         torch.cuda.synchronize()
         ms_total = sum(a0.elapsed_time(a1) for a0, a1 in evs)
     if dist:
         dist.barrier()
     launches = basalto.launch_count() - n0
-    mj1 = energy.read()
     clk = clocks.stop()
-    joules = (mj1 - mj0) / 1e3 if mj0 is not None and mj1 is not None else float("nan")
-    if dist:
-        t = torch.tensor([joules], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        joules = float(t.item())
     if dist:
         t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -430,15 +586,62 @@ def run_basalto(args):
     ms_step = ms_total / args.steps
     value = points_job * sweeps * args.steps / (ms_total * 1e-3) / 1e9
 
-    # Dominant kernel: the sweep itself; average launch = timed region / sweeps (per rank).
-    # Multi-sweep runs fuse several sweeps per launch (temporal blocking); each launch still
-    # reads its input grid once and writes its output once, so the algorithmic traffic of a
-    # launch is 2 * elem bytes per point whatever the number of sweeps it fuses.
-    # At N > 1 a pass over the slab is split into boundary and interior launches: the unit is
-    # the pass (all of this rank's points once), timed over the whole region.
-    passes = launches if ws == 1 else slab_passes * args.steps
+    # ---- parity of the last timed step's result ----------------------------------------------
+    basalto.check_device_errors(local)
+    bad, checked = 0, 0
+    for p, box, lo_box in check:
+        if prog.boundary == "zero":
+            want = oracle_at_point(box, lo_box, gshape, p, prog, sweeps)
+            if sharded:
+                got = result[(p[0] - my_start + G,) + tuple(p[1:])].item()
+            else:
+                got = result[p].item()
+        else:
+            from oracle import stencil_oracle as O
+            want = O.eval_program(box, [(t.op, t.scale, t.taps) for t in prog.terms], prog.init_zero, "valid",
+                                  prog.shrink)[0]
+            got = result[p].item()
+        checked += 1
+        if not (np.array_equal(np.asarray(want), np.asarray(got, dtype=box.dtype))):
+            bad += 1
+    if dist:
+        t = torch.tensor([bad, checked], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        bad, checked = int(t[0].item()), int(t[1].item())
+    parity = {"ok": bad == 0 and checked > 0, "points": checked, "mismatches": bad,
+              "against": "CPU oracle (oracle/stencil_oracle.py) folded over each point's input neighbourhood, "
+                         "bit for bit, after the last timed step"}
+
+    # ---- energy over at least one second of steps ----------------------------------------
+    energy = None
+    meter = EnergyMeter(local)
+    if meter.nv is not None:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        mj0, t0, n_e = meter.read(), time.perf_counter(), 0
+        while n_e < args.steps or time.perf_counter() - t0 < 1.0:
+            step()
+            n_e += 1
+            if n_e % 4 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        mj1 = meter.read()
+        joules = (mj1 - mj0) / 1e3 if mj0 is not None and mj1 is not None else float("nan")
+        t = torch.tensor([joules, n_e], dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            joules = float(t[0].item())
+            n_e = int(t[1].item()) // ws
+        if joules == joules and joules > 0:
+            energy = {"joules_per_step": round(joules / n_e, 4),
+                      "gpts_per_joule": round(points_job * sweeps * n_e / joules / 1e9, 3),
+                      "steps": n_e, "note": "NVML total-energy counter, summed over GPUs, untimed steps"}
+
+    # Dominant kernel: the sweep; per pass over this rank's grid.
+    passes = launches if not sharded else slab_passes * args.steps
     launch_ms = ms_total / max(1, passes)
-    per_launch_bytes = 2 * es * w.points
+    per_launch_bytes = 2 * es * local_points
     achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
     peak, peak_src = _peaks()
     if w.name.startswith("mean3"):
@@ -448,78 +651,40 @@ def run_basalto(args):
     else:
         kernel = "march_tma_kernel"
 
-    # ---- e2e through the public API with host buffers ---------------------------------------
-    e2e = None
-    if ws == 1 and args.e2e_steps > 0:
-        host_in = w.make_input().pin_memory()
-        host_out = torch.empty(prog.out_shape(w.shape), dtype=w.dtype).pin_memory()
-
-        def timed(step_fn):
-            step_fn()
-            torch.cuda.synchronize()
-            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            f0.record(stream)
-            for _ in range(args.e2e_steps):
-                step_fn()
-            f1.record(stream)
-            torch.cuda.synchronize()
-            return f0.elapsed_time(f1) / args.e2e_steps
-
-        # (1) the multi-sweep call (basalto.sweeps -> bst_stencil_sweeps), host in and out, two
-        #     steps in flight (uploads and downloads overlap the sweeps of the neighbouring steps)
-        ea = [torch.empty(w.shape, dtype=w.dtype, device=dev) for _ in range(2)]
-        eb = [torch.empty(prog.out_shape(w.shape), dtype=w.dtype, device=dev) for _ in range(2)]
-        res = [None, None]
-        outs = [host_out, torch.empty_like(host_out).pin_memory()]
-
-        def up(s):
-            ea[s].copy_(host_in, non_blocking=True)
-
-        def comp(s):
-            if prog.boundary == "zero":
-                res[s] = basalto.sweeps(prog, ea[s], eb[s], sweeps)
-            else:
-                res[s] = basalto.apply(prog, ea[s], out=eb[s])
-
-        def down(s):
-            outs[s].copy_(res[s], non_blocking=True)
-
-        e_ms = pipelined(args.e2e_steps, up, comp, down, stream)
-        e2e = {"value": round(w.points * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
-               "h2d_bytes_per_step": w.points * es, "d2h_bytes_per_step": w.out_points * es,
-               "ms_per_step": round(e_ms, 3),
-               "path": "basalto.sweeps (C ABI bst_stencil_sweeps), pinned host grid copied in and out each step; "
-                       "two steps in flight on separate copy streams"}
-        # (2) the drop-in plugin: torch.compile(backend="basalto") called once per sweep
-        torch._dynamo.reset()
-        cf = torch.compile(w.fn, backend="basalto")
-
-        def e2e_plugin():
-            x = host_in.to(dev, non_blocking=True)
-            for _ in range(sweeps):
-                x = cf(x)
-            host_out.copy_(x, non_blocking=True)
-
-        p_ms = timed(e2e_plugin)
-        e2e["torch_compile_per_sweep"] = {"value": round(w.points * sweeps / (p_ms * 1e-3) / 1e9, 4),
-                                          "ms_per_step": round(p_ms, 3)}
-
+    # ---- per-pass breakdown and halo bandwidth (N > 1) ---------------------------------------
+    pass_times = None
     halo = None
-    if ws > 1:
+    if sharded:
+        torch.cuda.synchronize()
+        dist.barrier()
+        _abi.check(lib.bst_comm_profile_begin(comm, 2 * slab_passes))
+        for _ in range(2):
+            step()
+        out = (ctypes.c_double * 6)()
+        _abi.check(lib.bst_comm_profile_end(comm, out))
+        v = torch.tensor(list(out), dtype=torch.float64, device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        npass = max(1.0, float(v[4].item()))
+        pass_times = {"boundary_ms": round(float(v[0].item()) / npass, 4),
+                      "exchange_ms": round(float(v[1].item()) / npass, 4),
+                      "interior_ms": round(float(v[2].item()) / npass, 4),
+                      "span_ms": round(float(v[3].item()) / npass, 4),
+                      "exposed_exchange_ms": round(float(v[5].item()) / npass, 4),
+                      "passes": int(npass),
+                      "note": "per pass, CUDA events on the boundary, comm and compute streams, two untimed steps, "
+                              "max over ranks; exposed = exchange time left after the interior launch ended"}
         # NVLink halo bandwidth: one ghost exchange (G planes each way per neighbour) timed on
-        # the device.  A ~1 ms sleep kernel ahead of it keeps the GPU busy while the host
-        # enqueues the NCCL group, so the events bracket the exchange itself, not the host.
-        n_ex = 10
+        # the device.  A sleep kernel ahead of it keeps the GPU busy while the host enqueues the
+        # NCCL group, so the events bracket the exchange itself, not the host.
         times = []
-        for _ in range(n_ex):
+        for _ in range(10):
             torch.cuda.synchronize()
             dist.barrier()
             h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            if hasattr(torch.cuda, "_sleep"):  # keeps the GPU busy while the host enqueues
+            if hasattr(torch.cuda, "_sleep"):
                 torch.cuda._sleep(2_000_000)
             h0.record(stream)
-            _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, local_shape[0],
-                                                    G, sp))
+            _abi.check(lib.bst_halo_exchange(comm, ctypes.c_void_p(a.data_ptr()), dt, plane, n_local, G, sp))
             h1.record(stream)
             torch.cuda.synchronize()
             t = torch.tensor([h0.elapsed_time(h1)], dtype=torch.float64, device=dev)
@@ -529,41 +694,97 @@ def run_basalto(args):
         nbrs = min(2, ws - 1)  # an interior rank's neighbours (an end rank's at N = 2)
         ex_bytes = 2 * nbrs * G * plane * es  # sent + received by that rank
         halo = {"ghost_planes": G, "bytes_per_exchange": ex_bytes, "exchange_ms": round(ex_ms, 4),
-                "nvlink_gbs": round(ex_bytes / (ex_ms * 1e-3) / 1e9, 2),
-                "exchanges_per_step": slab_passes,
+                "nvlink_gbs": round(ex_bytes / (ex_ms * 1e-3) / 1e9, 2), "exchanges_per_step": slab_passes,
                 "note": "one exchange timed on the device after a sleep kernel hides its host enqueue "
                         "(median of 10, max over ranks); in the sweep loop it overlaps the interior launch"}
 
-    if ws > 1 and args.e2e_steps > 0:
-        # The slab API with host buffers: each step copies this rank's slab in from pinned host
-        # memory, exchanges ghosts, runs the sweeps and copies the owned result back.
-        host_in = (torch.rand(local_shape, generator=torch.Generator().manual_seed(w.seed + rank), dtype=w.dtype)
-                   * 2 - 1).pin_memory()
-        outs = [torch.empty(local_shape, dtype=w.dtype).pin_memory() for _ in range(2)]
-        sa = [a, torch.zeros_like(a)]
-        sb = [b, torch.zeros_like(b)]
-        nl = local_shape[0]
+    # ---- e2e through the public API with host buffers ---------------------------------------
+    e2e = None
+    if args.e2e_steps > 0 and not sharded:
+        host_in = x0.cpu().pin_memory()
+        out_shape = prog.out_shape(x0.shape)
+        outs = [torch.empty(out_shape, dtype=w.dtype).pin_memory() for _ in range(2)]
+        ex = [torch.empty_like(x0) for _ in range(2)]
+        ea = [torch.empty(out_shape, dtype=w.dtype, device=dev) if prog.boundary == "zero" else None for _ in range(2)]
+        eb = [torch.empty(out_shape, dtype=w.dtype, device=dev) for _ in range(2)]
+        res = [None, None]
 
         def up(s):
-            sa[s][G:G + nl].copy_(host_in, non_blocking=True)
+            ex[s].copy_(host_in, non_blocking=True)
 
         def comp(s):
-            _abi.check(_abi.lib().bst_halo_exchange(comm, ctypes.c_void_p(sa[s].data_ptr()), dt, plane, nl, G, sp))
-            _abi.check(_abi.lib().bst_slab_sweeps_deep(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
-                                                       ctypes.c_void_p(sa[s].data_ptr()),
-                                                       ctypes.c_void_p(sb[s].data_ptr()), sweeps, sp))
+            res[s] = step_on(ex[s], ea[s], eb[s])
 
         def down(s):
-            res = sa[s] if sweeps % 2 == 0 else sb[s]
-            outs[s].copy_(res[G:G + nl], non_blocking=True)
+            outs[s].copy_(res[s], non_blocking=True)
+
+        e_ms = pipelined(args.e2e_steps, up, comp, down, stream)
+        if dist:
+            t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": round(points_job * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
+               "h2d_bytes_per_step": w.points * es * max(1, ws), "d2h_bytes_per_step": w.out_points * es * max(1, ws),
+               "ms_per_step": round(e_ms, 3),
+               "path": "basalto.apply + basalto.sweeps (C ABI bst_stencil_apply + bst_stencil_sweeps), pinned host "
+                       "grid copied in and the result copied out every step; two steps in flight on separate copy "
+                       "streams" + ("; every rank a replica, max over ranks" if ws > 1 else "")}
+        del ex, ea, eb
+        torch.cuda.empty_cache()
+        if ws == 1:
+            # the drop-in plugin: torch.compile(backend="basalto") called once per sweep
+            torch._dynamo.reset()
+            cf = torch.compile(w.fn, backend="basalto")
+            host_out = outs[0]
+
+            def e2e_plugin():
+                x = host_in.to(dev, non_blocking=True)
+                y = x
+                for _ in range(sweeps):
+                    y = cf(y if prog.boundary == "zero" else x)
+                host_out.copy_(y, non_blocking=True)
+
+            e2e_plugin()
+            torch.cuda.synchronize()
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(args.e2e_steps):
+                e2e_plugin()
+            f1.record(stream)
+            torch.cuda.synchronize()
+            p_ms = f0.elapsed_time(f1) / args.e2e_steps
+            e2e["torch_compile_per_sweep"] = {"value": round(w.points * sweeps / (p_ms * 1e-3) / 1e9, 4),
+                                              "ms_per_step": round(p_ms, 3)}
+    elif args.e2e_steps > 0 and sharded:
+        # The slab API with host buffers: each step copies this rank's owned planes in from
+        # pinned host memory, exchanges their ghosts, runs the sweeps and copies the owned
+        # result back.
+        host_in = x0[G:G + n_local].cpu().pin_memory()
+        outs = [torch.empty(local_shape, dtype=w.dtype).pin_memory() for _ in range(2)]
+        sx = [x0, torch.zeros_like(x0)]
+        sa = [a, torch.zeros_like(a)]
+        sb = [b, torch.zeros_like(b)]
+        res = [None, None]
+
+        def up(s):
+            sx[s][G:G + n_local].copy_(host_in, non_blocking=True)
+
+        def comp(s):
+            st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+            _abi.check(lib.bst_halo_exchange(comm, ctypes.c_void_p(sx[s].data_ptr()), dt, plane, n_local, G, st))
+            res[s] = step_on(sx[s], sa[s], sb[s])
+
+        def down(s):
+            outs[s].copy_(res[s][G:G + n_local], non_blocking=True)
 
         torch.cuda.synchronize()
         dist.barrier()
         t = torch.tensor([pipelined(args.e2e_steps, up, comp, down, stream)], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
+        total_bytes = int(np.prod(gshape)) * es
         e2e = {"value": round(points_job * sweeps / (e_ms * 1e-3) / 1e9, 4), "unit": UNIT,
-               "h2d_bytes_per_step": w.points * es * ws, "d2h_bytes_per_step": w.points * es * ws,
+               "h2d_bytes_per_step": total_bytes, "d2h_bytes_per_step": total_bytes,
                "ms_per_step": round(e_ms, 3),
                "path": "bst_halo_exchange + bst_slab_sweeps_deep per rank, pinned host slab copied in and out "
                        "each step (bytes summed over ranks), two steps in flight, max over ranks"}
@@ -572,23 +793,25 @@ def run_basalto(args):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        r, dt, n = CpuReference(w, threads).rate_for(args.cpu_seconds, cap=100000)
+        ref = CpuReference(w, threads)
+        r, secs, n = ref.rate_for(args.cpu_seconds)
         cpu = {"value": round(r, 4), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{n} consecutive sweeps ({dt:.1f} s) on the full {'x'.join(map(str, w.shape))} grid "
-                         f"({sweeps} sweeps per step), eager torch via the reference backend's control flow"}
+               "sample": f"{n} sweeps ({secs:.1f} s): " + ref.describe()}
 
     if comm is not None:
         torch.cuda.synchronize()
-        _abi.lib().bst_comm_destroy(comm)
+        lib.bst_comm_destroy(comm)
 
     if rank == 0:
+        scaling = "weak" if w.scaling in ("weak", "replicas") else "strong"
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32" if w.dtype == torch.float32 else "f64", "data": "synthetic",
-            "config": {"workload": f"{w.name} {'x'.join(map(str, w.shape))}{' per GPU' if ws > 1 else ''}, "
-                                   f"{sweeps} sweeps per step",
-                       "parallelism": f"z-slab x{ws}" if ws > 1 else "single GPU",
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": _dtype_name(w), "data": "synthetic",
+            "config": {"workload": w.label(),
+                       "global_grid": "x".join(map(str, gshape)),
+                       "parallelism": (f"z-slab x{ws} ({scaling} scaling, {G} ghost planes per side)" if sharded
+                                       else (f"{ws} independent replicas" if ws > 1 else "single GPU")),
                        "arithmetic": "fused multiply-add fold (BST_PROGRAM_CONTRACT)" if w.program.contract
                        else "separately rounded (bit-identical to eager torch)",
                        "l2": l2_note},
@@ -597,39 +820,37 @@ def run_basalto(args):
                          "frac_of_nominal_8000": round(achieved / 8000.0, 4),
                          "kernel": kernel, "traffic": _traffic(w.name, kernel),
                          "algorithmic_bytes_per_launch": per_launch_bytes, "avg_launch_ms": round(launch_ms, 5)},
+            "parity": parity,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
-            "energy": {"joules_per_step": round(joules / args.steps, 4),
-                       "gpts_per_joule": round(points_job * sweeps * args.steps / joules / 1e9, 3)}
-                      if joules == joules and joules > 0 else None,
-            "halo": halo,
-            "sweeps_per_launch": round(sweeps * args.steps / max(1, launches), 3),
+            "energy": energy, "passes": pass_times, "halo": halo,
+            "sweeps_per_launch": round(sweeps * args.steps / max(1, passes), 3),
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+    if not parity["ok"]:
+        raise SystemExit(f"parity check failed: {bad} of {checked} sampled points differ from the oracle")
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="basalto", choices=["basalto", "reference"])
-    ap.add_argument("--workload", default="jacobi5_2d")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--contract", action="store_true",
                     help="fold multiplied terms with fused multiply-add (BST_PROGRAM_CONTRACT) instead of "
                          "rounding every operation separately")
     ap.add_argument("--dtype", choices=["f32", "f64"], default=None,
                     help="override the workload's dtype (e.g. the 27-point box in fp32)")
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
-    ap.add_argument("--ref-sweeps", type=int, default=3, help="sweeps per step of --impl reference")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--host-input", action="store_true", default=True)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -98,6 +98,8 @@ SIGNATURES = [
     ("bst_slab_sweeps_deep", c_int32,
      [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
       c_void_p]),
+    ("bst_comm_profile_begin", c_int32, [c_void_p, c_int32]),
+    ("bst_comm_profile_end", c_int32, [c_void_p, POINTER(c_double)]),
 ]
 
 _lib = None

@@ -12,6 +12,11 @@ generator seeded 3.
   heat7_3d    0.4*u + 0.1*(6 neighbours) fp32 512^3 ~U(0,1) seed 2, zero ghosts, 50 steps
   box27_3d    27 weights ~U(0,1/27), fp64 768^3 ~N(0,1) seed 3, zero ghosts, 20 steps
   star25_3d   8th-order Laplacian star r=4, fp32 1024^3 ~N(0,1) seed 4, zero ghosts, 10 steps
+
+`scaling` says how a workload spreads over N GPUs (Z-slabs along axis 0): "strong" splits
+the one global grid (heat-7 512^3, star-25 1024^3), "weak" gives every GPU a grid of the
+listed size (box-27 768^3 per GPU; the 2-D Jacobi grid), "replicas" runs independent copies
+(the 1-D mean, which has no slab axis).
 """
 from __future__ import annotations
 
@@ -106,6 +111,22 @@ class Workload:
     dist: str
     seed: int
     steps: int
+    scaling: str = "strong"   # "strong" | "weak" | "replicas" across GPUs
+
+    def global_shape(self, nranks: int = 1) -> tuple[int, ...]:
+        """The grid all ranks together hold: the listed grid (strong, replicas) or nranks
+        of them stacked along axis 0 (weak)."""
+        if self.scaling == "weak" and nranks > 1:
+            return (self.shape[0] * nranks,) + tuple(self.shape[1:])
+        return tuple(self.shape)
+
+    def label(self) -> str:
+        """One name for the configuration, the same in every measurement that runs it."""
+        dt = "fp32" if self.dtype == torch.float32 else "fp64"
+        per = " per GPU" if self.scaling == "weak" else ""
+        return (f"{self.name} {'x'.join(map(str, self.shape))}{per} {dt} {self.dist} seed {self.seed}, "
+                f"{self.steps} sweep{'s' if self.steps != 1 else ''} per step"
+                f"{' from the unchanged seeded grid' if self.program.boundary == 'zero' else ''}")
 
     @property
     def points(self) -> int:
@@ -132,14 +153,16 @@ class Workload:
 def _workloads() -> dict[str, Workload]:
     w27 = box27_weights(3)
     return {
-        "mean3_1d": Workload("mean3_1d", mean3_1d, P.mean3_1d(), (1 << 24,), torch.float32, "randn", 0, 1),
+        "mean3_1d": Workload("mean3_1d", mean3_1d, P.mean3_1d(), (1 << 24,), torch.float32, "randn", 0, 1,
+                             "replicas"),
         "jacobi5_2d": Workload("jacobi5_2d", jacobi5_2d, P.jacobi5_2d(), (8192, 8192), torch.float32,
-                               "rand_pm1", 1, 100),
-        "heat7_3d": Workload("heat7_3d", heat7_3d, P.heat7_3d(), (512, 512, 512), torch.float32, "rand", 2, 50),
+                               "rand_pm1", 1, 100, "weak"),
+        "heat7_3d": Workload("heat7_3d", heat7_3d, P.heat7_3d(), (512, 512, 512), torch.float32, "rand", 2, 50,
+                             "strong"),
         "box27_3d": Workload("box27_3d", make_box27_3d(w27), P.box(3, 1, w27), (768, 768, 768), torch.float64,
-                             "randn", 3, 20),
+                             "randn", 3, 20, "weak"),
         "star25_3d": Workload("star25_3d", make_star_3d(), P.star_3d(P.LAPLACIAN8_COEFFS), (1024, 1024, 1024),
-                              torch.float32, "randn", 4, 10),
+                              torch.float32, "randn", 4, 10, "strong"),
     }
 
 

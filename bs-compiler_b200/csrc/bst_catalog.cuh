@@ -127,9 +127,12 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 #ifndef BST_STAR_RB
 #define BST_STAR_RB 2  // two planes per stage: half the per-group bookkeeping per plane
 #endif
+#ifndef BST_STAR_PAIR
+#define BST_STAR_PAIR 0  // fp32 points two at a time (paired add/mul)
+#endif
 template <typename T, class S>
 using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX, bool(BST_STAR_HALO_LDS),
-                         false, bool(BST_STAR_WINDOW)>;
+                         false, bool(BST_STAR_WINDOW), 1, bool(BST_STAR_PAIR)>;
 // Boxes in ascending order stream: each input plane is applied to every output it touches as
 // it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
 #ifndef BST_BOXS_TY

@@ -87,6 +87,38 @@ unsigned* device_error_word() {
   return words[dev];
 }
 
+// Runtime-table programs resident on each device (launch_direct_table).  Keyed by the
+// table's bytes: FNV-1a digest first, then a full comparison.
+const void* cached_device_table(const void* blob, size_t bytes) {
+  struct Entry {
+    std::vector<unsigned char> host;
+    void* dev;
+  };
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, std::vector<Entry>> cache[64];
+  static int count[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  const unsigned char* b = static_cast<const unsigned char*>(blob);
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < bytes; ++i) h = (h ^ b[i]) * 1099511628211ull;
+  std::lock_guard<std::mutex> lk(mu);
+  auto& bucket = cache[dev][h];
+  for (const Entry& e : bucket)
+    if (e.host.size() == bytes && std::memcmp(e.host.data(), b, bytes) == 0) return e.dev;
+  if (count[dev] >= kTableCacheMax) return nullptr;
+  void* d = nullptr;
+  if (cudaMalloc(&d, bytes) != cudaSuccess) return nullptr;
+  // Synchronous copy: the entry is complete before any stream can launch with it.
+  if (cudaMemcpy(d, b, bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(d);
+    return nullptr;
+  }
+  bucket.push_back(Entry{std::vector<unsigned char>(b, b + bytes), d});
+  ++count[dev];
+  return d;
+}
+
 int check_device_error(cudaStream_t st) {
   unsigned* w = device_error_word();
   if (!w) return fail(BST_ERR_CUDA, "device error word unavailable");

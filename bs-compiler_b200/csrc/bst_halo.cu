@@ -14,6 +14,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "bst_internal.h"
 
@@ -97,6 +98,10 @@ struct bst_comm {
   // interior launch of the same pass.
   cudaStream_t bnd_stream = nullptr;
   cudaEvent_t ev_b[2] = {nullptr, nullptr}, ev_int = nullptr;
+  // Optional per-pass timing (bst_comm_profile_begin/end): six timing events per pass —
+  // boundary start/end, exchange start/end, interior start/end.
+  std::vector<cudaEvent_t> prof;
+  int prof_cap = 0, prof_used = 0;
 };
 
 namespace bst {
@@ -121,7 +126,21 @@ static int wait_comm(bst_comm* c, const char* what) {
 }
 }  // namespace bst
 
+static void release_profile(bst_comm* c) {
+  for (cudaEvent_t ev : c->prof)
+    if (ev) cudaEventDestroy(ev);
+  c->prof.clear();
+  c->prof_cap = c->prof_used = 0;
+}
+
+// Records timing event `which` (0..5) of the next profiled pass on `st` (no-op when off).
+static cudaError_t prof_mark(bst_comm* c, int which, cudaStream_t st) {
+  if (c->prof_used >= c->prof_cap) return cudaSuccess;
+  return cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + which], st);
+}
+
 static void release_cuda(bst_comm* c) {
+  release_profile(c);
   if (c->ev_bnd) cudaEventDestroy(c->ev_bnd);
   if (c->ev_comm) cudaEventDestroy(c->ev_comm);
   for (cudaEvent_t& ev : c->ev_b)
@@ -337,8 +356,11 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   const std::vector<int> plan = fuse_plan(nsteps, kmax);
   int kbig = 1;
   for (int kk : plan) kbig = kk > kbig ? kk : kbig;
-  const int64_t gx = int64_t(kbig) * R;  // planes exchanged per launch: the deepest read
-  if (c->nranks > 1 && nl < gx) return fail(BST_ERR_INVALID, "each rank must own at least (fused sweeps x radius) planes");
+  if (int64_t(kbig) * R > ghost) return fail(BST_ERR_INVALID, "fused sweeps read beyond the ghost planes");
+  // Every pass refreshes all `ghost` planes per side, so the result's ghosts are complete and a
+  // later call may fuse as deeply as the ghost depth allows, whatever this call fused.
+  const int64_t gx = ghost;
+  if (c->nranks > 1 && nl < gx) return fail(BST_ERR_INVALID, "each rank must own at least `ghost` planes");
   const size_t es = dtype == BST_F64 ? 8 : 4;
   // Intermediate levels are real data everywhere except beyond the global ends.
   const int64_t big = int64_t(1) << 40;
@@ -349,8 +371,6 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   char* src = static_cast<char*>(a);
   char* dst = static_cast<char*>(b);
   const size_t ghost_bytes = size_t(ghost) * plane * es;
-  // The exchange carries the planes [ghost - gx, ghost) below and above the owned range.
-  const size_t skip_bytes = size_t(ghost - gx) * plane * es;
   const int64_t lo_end = std::min<int64_t>(gx, nl);
   const int64_t hi_begin = std::max<int64_t>(nl - gx, lo_end);
   // Per pass k (src -> dst): the boundary rows run on the high-priority boundary stream,
@@ -366,21 +386,34 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
     void* out = dst + ghost_bytes;
     BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
     if (k > 0 && exchange) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
+    BST_CUDA(prof_mark(c, 0, c->bnd_stream));
     rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
     if (!rc && hi_begin < nl)
       rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd_stream);
     if (rc) return rc;
+    BST_CUDA(prof_mark(c, 1, c->bnd_stream));
     BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
     if (exchange) {
       BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
-      rc = halo_enqueue(c, dst + skip_bytes, dtype, plane, nl, int32_t(gx), c->comm_stream);
+      BST_CUDA(prof_mark(c, 2, c->comm_stream));
+      rc = halo_enqueue(c, dst, dtype, plane, nl, int32_t(gx), c->comm_stream);
       if (rc) return rc;
+      BST_CUDA(prof_mark(c, 3, c->comm_stream));
       BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
     }
     if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
+    BST_CUDA(prof_mark(c, 4, st));
     if (lo_end < hi_begin) {
       rc = launch_fused(k_canon, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
       if (rc) return rc;
+    }
+    BST_CUDA(prof_mark(c, 5, st));
+    if (c->prof_used < c->prof_cap) {
+      if (!exchange) {  // no exchange: a zero-length exchange interval at the boundary's end
+        BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 2], c->bnd_stream));
+        BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 3], c->bnd_stream));
+      }
+      ++c->prof_used;
     }
     BST_CUDA(cudaEventRecord(c->ev_int, st));
     std::swap(src, dst);
@@ -391,6 +424,57 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
     if (exchange) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
   }
   return BST_OK;
+}
+
+int bst_comm_profile_begin(bst_comm* c, int32_t max_passes) {
+  clear_error();
+  if (!c) return fail(BST_ERR_INVALID, "null communicator");
+  if (max_passes < 1 || max_passes > (1 << 16)) return fail(BST_ERR_INVALID, "max_passes must be in 1..65536");
+  BST_CUDA(cudaSetDevice(c->device));
+  release_profile(c);
+  c->prof.assign(size_t(max_passes) * 6, nullptr);
+  for (cudaEvent_t& ev : c->prof) {
+    cudaError_t e = cudaEventCreate(&ev);
+    if (e != cudaSuccess) {
+      release_profile(c);
+      return cuda_fail(e, "profiling events");
+    }
+  }
+  c->prof_cap = max_passes;
+  c->prof_used = 0;
+  return BST_OK;
+}
+
+int bst_comm_profile_end(bst_comm* c, double out[6]) {
+  clear_error();
+  if (!c || !out) return fail(BST_ERR_INVALID, "null argument");
+  for (int i = 0; i < 6; ++i) out[i] = 0.0;
+  if (c->prof_cap == 0) return fail(BST_ERR_INVALID, "profiling was not started");
+  BST_CUDA(cudaSetDevice(c->device));
+  int rc = BST_OK;
+  for (int p = 0; p < c->prof_used && rc == BST_OK; ++p) {
+    cudaEvent_t* e = &c->prof[size_t(p) * 6];
+    float t_b = 0, t_x = 0, t_i = 0, t_end_i = 0, t_end_x = 0;
+    cudaError_t err = cudaEventSynchronize(e[5]);
+    if (err == cudaSuccess) err = cudaEventSynchronize(e[3]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t_b, e[0], e[1]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t_x, e[2], e[3]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t_i, e[4], e[5]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t_end_i, e[0], e[5]);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&t_end_x, e[0], e[3]);
+    if (err != cudaSuccess) {
+      rc = cuda_fail(err, "reading the profiling events");
+      break;
+    }
+    out[0] += t_b;
+    out[1] += t_x;
+    out[2] += t_i;
+    out[3] += t_end_i > t_end_x ? t_end_i : t_end_x;  // pass span: boundary start to last end
+    out[5] += t_end_x - t_end_i > 0 ? t_end_x - t_end_i : 0;  // exchange left over after the interior
+  }
+  out[4] = double(c->prof_used);
+  release_profile(c);
+  return rc;
 }
 
 int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,

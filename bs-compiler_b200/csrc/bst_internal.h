@@ -68,6 +68,14 @@ std::vector<int> fuse_plan(int nsteps, int kmax);
 enum class Schedule { kItems, kLockstep, kBalanced };
 Schedule march_schedule();
 
+// Device copies of runtime-table programs, uploaded once per device and shared by every later
+// call that carries the same table bytes: the repeat path makes no allocation, no copy and no
+// host synchronisation.  A miss allocates and copies synchronously (once per program); the
+// entries live until the process exits, at most kTableCacheMax per device.  Returns nullptr
+// when the cache is full or the upload failed (the caller then uploads for one call).
+constexpr int kTableCacheMax = 256;
+const void* cached_device_table(const void* blob, size_t bytes);
+
 // Device error word (kernels OR bits into it); allocated once per device.
 unsigned* device_error_word();
 // Reads and clears the calling device's error word (synchronizes the stream).

@@ -17,6 +17,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <type_traits>
 #include <utility>
 
 #include "bst_shapes.cuh"
@@ -192,7 +193,7 @@ constexpr auto pick_segs() {
 // ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
 // wide radii, dearer in shared-memory bandwidth.
 template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false,
-          bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1>
+          bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1, bool PAIR_ = false>
 struct MarchCfg {
   using shape = S;
   static constexpr int MINB = MINB_;  // CTAs per SM the register allocation must allow
@@ -218,6 +219,11 @@ struct MarchCfg {
   // and the configuration asks for it; otherwise every tap is read from the shared ring.
   static constexpr bool WINDOW = WINDOW_ && window_mode<S>();
   static constexpr int WM = WINDOW ? window_depth<S>() : 0;
+  // Window slots: a group of RB plane steps reads planes g0-WM .. g0+RB-1+WM (g0 = the group's
+  // first output plane), so the window holds 2WM+RB planes and shifts by RB once per group.
+  static constexpr int WSLOTS = WINDOW ? 2 * WM + RB : 1;
+  // fp32 points evaluated two at a time with paired instructions (gather mode only).
+  static constexpr bool PAIR = PAIR_ && sizeof(T) == 4 && !STREAM;
   // Stages read by group g (input planes g*RB + [0, RB-1+2RM] relative to the item's first
   // loaded plane): the window keeps planes behind the current one in registers, so in window
   // mode group g only reads from plane g*RB + RM on and earlier stages retire early.
@@ -289,18 +295,19 @@ struct Vec16<double> {
 // Per-thread register state of the march: window and row segments.
 template <typename T, class C>
 struct MarchRegs {
-  T win[2 * C::WM + 1][C::PY][C::VX];
+  T win[C::WSLOTS][C::PY][C::VX];
   T seg[C::NSEG > 0 ? C::NSEG : 1][C::SEGW];
   T acc[C::STREAM ? 2 * C::RM + 1 : 1][C::PY][C::VX];  // stream mode: outputs g .. g+2RM in flight
 };
 
-template <typename T, class C, int J, int V>
+// Tap values of point (row J, element V) at plane step P of a group.
+template <typename T, class C, int J, int V, int P = 0>
 struct PointFetch {
   const MarchRegs<T, C>& r;
   template <int dm, int dy, int dx>
   __device__ __forceinline__ T get() const {
     if constexpr (C::WINDOW && (dm != 0 || (dy == 0 && dx == 0))) {
-      return r.win[C::WM + dm][J][V];
+      return r.win[P + C::WM + dm][J][V];
     } else if constexpr (C::STREAM) {  // every offset reads the current lead plane's rows
       constexpr int k = C::seg_index(C::RM, J + dy);
       static_assert(k >= 0, "tap without a row segment");
@@ -322,16 +329,17 @@ __device__ __forceinline__ void lds_vec(const T* p, T (&v)[N]) {
   for (int i = 0; i < N; ++i) v[i] = e[i];
 }
 
-// Load row segment K for the plane whose tile starts at `pl` (dm already applied).
-// `pl` points at the thread's first vector (row 0 of its rows) in the plane tile.
-template <typename T, class C, int K>
+// Load row segment K for the plane whose tile starts at `pl` (dm already applied), at plane
+// step P of a group.  `pl` points at the thread's first vector (row 0 of its rows) in the
+// plane tile.
+template <typename T, class C, int K, int P = 0>
 __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, int /*unused*/, int lane_x) {
   constexpr SegRow R = C::SEGS.r[K];
   const T* rowp = pl + R.srow * C::TXL;
   T own[C::VX];
   if constexpr (C::WINDOW && R.dm == 0 && R.srow >= 0 && R.srow < C::PY) {
 #pragma unroll
-    for (int e = 0; e < C::VX; ++e) own[e] = r.win[C::WM][R.srow][e];
+    for (int e = 0; e < C::VX; ++e) own[e] = r.win[P + C::WM][R.srow][e];
   } else {
     lds_vec<T, C::VX>(rowp, own);
   }
@@ -370,24 +378,65 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
   }
 }
 
-template <typename T, class C, int J, int... Vs>
-__device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c, T (&res)[C::VX],
+// Tap values of the points (row J, elements V and V+1) as one pair (PAIR configurations).
+template <class C, int J, int V, int P>
+struct PairFetch {
+  const MarchRegs<float, C>& r;
+  template <int dm, int dy, int dx>
+  __device__ __forceinline__ float2 get() const {
+    return make_float2(PointFetch<float, C, J, V, P>{r}.template get<dm, dy, dx>(),
+                       PointFetch<float, C, J, V + 1, P>{r}.template get<dm, dy, dx>());
+  }
+};
+
+// The coefficient set a configuration evaluates with: pairs of equal scales for PAIR.
+template <typename T, class C>
+using EvalCoefs = std::conditional_t<C::PAIR, Coefs<float2, C::shape::NTERMS>, Coefs<T, C::shape::NTERMS>>;
+
+template <typename T, class C>
+__device__ __forceinline__ EvalCoefs<T, C> eval_coefs(const Coefs<T, C::shape::NTERMS>& c) {
+  if constexpr (C::PAIR) {
+    Coefs<float2, C::shape::NTERMS> p;
+#pragma unroll
+    for (int g = 0; g < C::shape::NTERMS; ++g) p.scale[g] = make_float2(c.scale[g], c.scale[g]);
+    p.init_zero = c.init_zero;
+    return p;
+  } else {
+    return c;
+  }
+}
+
+template <typename T, class C, int P, int J, int... Vs>
+__device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const EvalCoefs<T, C>& c, T (&res)[C::VX],
                                          std::integer_sequence<int, Vs...>) {
-  ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs>{r}, c)), ...);
+  if constexpr (C::PAIR) {
+    static_assert(C::VX % 2 == 0, "whole pairs");
+    (
+        [&] {
+          if constexpr (Vs % 2 == 0) {
+            const float2 v = eval_shape<typename C::shape, float2>(PairFetch<C, J, Vs, P>{r}, c);
+            res[Vs] = v.x;
+            res[Vs + 1] = v.y;
+          }
+        }(),
+        ...);
+  } else {
+    ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs, P>{r}, c)), ...);
+  }
 }
 
 // Evaluate the PY x VX points of one plane step and store them.  `dst` points at the
 // thread's first output of row 0 of this plane; `interior` = the whole tile is inside the
 // output and rows are 16-byte aligned (unchecked vector stores).
-template <typename T, class C, int... Js>
-__device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+template <typename T, class C, int P, int... Js>
+__device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                            T* __restrict__ dst, long long so1, bool interior, int rows_left,
                                            int cols_left, long long so2, std::integer_sequence<int, Js...>) {
   using VT = typename Vec16<T>::type;
   (
       [&] {
         T res[C::VX];
-        eval_row<T, C, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
+        eval_row<T, C, P, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
         T* d = dst + Js * so1;
         if (interior) {
           VT q;
@@ -413,7 +462,7 @@ __device__ __forceinline__ const T* stage_plane(const T* const* sb) {
 template <typename T, class C, int P, int... Ks>
 __device__ __forceinline__ void load_segments_at(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                                  std::integer_sequence<int, Ks...>) {
-  (load_segment<T, C, Ks>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
+  (load_segment<T, C, Ks, P>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
 }
 
 // ---- stream mode -------------------------------------------------------------------
@@ -499,10 +548,11 @@ __device__ __forceinline__ void stream_store(const MarchRegs<T, C>& r, T* __rest
       ...);
 }
 
-// One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store, rotate.
+// One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store (the window
+// shifts once per group, in group_steps).
 template <typename T, class C, int P>
 __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
-                                           const Coefs<T, C::shape::NTERMS>& coef, T* dst, long long so1,
+                                           const EvalCoefs<T, C>& coef, T* dst, long long so1,
                                            bool interior, int rows_left, int cols_left, long long so2) {
   if constexpr (C::STREAM) {
     stream_rows<T, C, P + 2 * C::RM>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
@@ -518,25 +568,18 @@ __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* s
     if constexpr (C::WINDOW) {
       const T* pl = stage_plane<T, C, P + C::RM + C::WM>(sb) + toff;
 #pragma unroll
-      for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[2 * C::WM][j]);
+      for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[P + 2 * C::WM][j]);
     }
     if constexpr (C::NSEG > 0)
       load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
-    eval_store<T, C>(r, coef, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
-    if constexpr (C::WINDOW) {
-#pragma unroll
-      for (int k = 0; k < 2 * C::WM; ++k)
-#pragma unroll
-        for (int j = 0; j < C::PY; ++j)
-#pragma unroll
-          for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + 1][j][e];
-    }
+    eval_store<T, C, P>(r, coef, dst, so1, interior, rows_left, cols_left, so2,
+                        std::make_integer_sequence<int, C::PY>{});
   }
 }
 
 template <typename T, class C, int... Ps>
 __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
-                                            const Coefs<T, C::shape::NTERMS>& coef, T* dst0, long long so0,
+                                            const EvalCoefs<T, C>& coef, T* dst0, long long so0,
                                             long long so1, bool interior, int rows_left, int cols_left,
                                             long long so2, int planes, std::integer_sequence<int, Ps...>) {
   // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
@@ -544,6 +587,14 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
                                        cols_left, so2)
                 : void()),
    ...);
+  if constexpr (C::WINDOW) {  // next group: its planes g0+RB-WM .. are slots RB ..
+#pragma unroll
+    for (int k = 0; k < 2 * C::WM; ++k)
+#pragma unroll
+      for (int j = 0; j < C::PY; ++j)
+#pragma unroll
+        for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + C::RB][j][e];
+  }
 }
 
 template <typename T, class C>
@@ -573,6 +624,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
   int n_waited = 0;        // stages of the current item waited on so far
   bool failed = false;
   MarchRegs<T, C> r;
+  const EvalCoefs<T, C> ecoef = eval_coefs<T, C>(coef);
 
   const long long tiles = (long long)a.tiles_x * a.tiles_y;
   long long w_beg, w_end;
@@ -677,7 +729,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
       }
       const long long m_grp = (long long)grp * C::RB;
       const int planes = int(me - mb - m_grp);
-      group_steps<T, C>(r, sb, toff, lane_x, coef, out_item + m_grp * g.so[0], g.so[0], g.so[1], interior,
+      group_steps<T, C>(r, sb, toff, lane_x, ecoef, out_item + m_grp * g.so[0], g.so[0], g.so[1], interior,
                         rows_left, cols_left, g.so[2], planes, std::make_integer_sequence<int, C::RB>{});
     }
     if (failed) break;

@@ -201,7 +201,7 @@ __device__ __forceinline__ T fold_range(T acc, const F& f, const Coefs<T, S::NTE
 template <class S, class T, class F>
 __device__ __forceinline__ T eval_shape(const F& f, const Coefs<T, S::NTERMS>& c) {
   T acc = eval_term<S, 0, T>(f, c);
-  if (c.init_zero) acc = add_rn(T(0), acc);
+  if (c.init_zero) acc = add_rn(zero_of<T>(), acc);
   return fold_terms<S, T>(acc, f, c, std::make_integer_sequence<int, S::NTERMS - 1>{});
 }
 

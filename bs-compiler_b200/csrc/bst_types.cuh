@@ -68,6 +68,26 @@ __device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(
 __device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
 __device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
 
+// Two fp32 lanes per instruction (sm_100 paired add/mul/fma .f32x2).  CUDA documents each
+// component of __fadd2_rn / __fmul2_rn / __ffma2_rn as numerically identical to the scalar
+// __fadd_rn / __fmul_rn / __fmaf_rn, so a pair of points evaluated together rounds exactly as
+// two points evaluated apart.  There is no paired divide: its components divide separately.
+__device__ __forceinline__ float2 add_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul_rn(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 div_rn(float2 a, float2 b) {
+  return make_float2(__fdiv_rn(a.x, b.x), __fdiv_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 fma_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+template <typename T>
+__device__ __forceinline__ T zero_of() {
+  return T(0);
+}
+template <>
+__device__ __forceinline__ float2 zero_of<float2>() {
+  return make_float2(0.f, 0.f);
+}
+
 template <typename T>
 __device__ __forceinline__ T apply_op(int op, T scale, T s) {
   // torch: `c * t` and `t * c` are the same IEEE product; `t / c` is IEEE division.

@@ -245,7 +245,10 @@ BST_API int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype,
  * it fuses k <= min(kernel limit, ghost / R) sweeps per launch and exchanges k*R planes once
  * per k sweeps (boundary planes first, interior overlapped), so a run of n sweeps makes about
  * n/k exchanges instead of n.  Same result-buffer contract (b when nsteps is odd, a when even)
- * and the same bits as n single sweeps.  Each rank must own at least k*R planes.
+ * and the same bits as n single sweeps.  Every pass refreshes all `ghost` planes per side, so
+ * the result's ghosts are complete and a later call may fuse as deeply as `ghost` allows
+ * (a 1-sweep call followed by an n-sweep call equals one (n+1)-sweep call).  Each rank must
+ * own at least `ghost` planes.
  * bst_slab_ghost_depth reports the depth that allows the most fusion for this program and
  * local shape (R when nothing fuses).  Replaces the per-step exchange of
  * crates/basalto-tree/src/executor.rs:91-119 (one exchange per kernel launch). */
@@ -254,6 +257,17 @@ BST_API int bst_slab_ghost_depth(const bst_program* prog, int32_t dtype, int32_t
 BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
                                  const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
                                  void* stream);
+
+/* Per-pass timing of the slab sweeps (diagnostics).  After bst_comm_profile_begin, the next
+ * max_passes passes of bst_slab_sweeps_deep on this communicator record CUDA timing events
+ * around their boundary launches, their ghost exchange and their interior launch.
+ * bst_comm_profile_end waits for those events and returns, summed over the recorded passes:
+ * out[0] boundary-launch ms, out[1] exchange ms, out[2] interior-launch ms, out[3] pass span ms
+ * (boundary start to the later of interior end and exchange end), out[4] passes recorded,
+ * out[5] ms by which exchanges outlasted their interior launch (exposed exchange time).
+ * The reference times whole launches only (crates/basalto-tree/src/executor.rs:107-124). */
+BST_API int bst_comm_profile_begin(bst_comm* c, int32_t max_passes);
+BST_API int bst_comm_profile_end(bst_comm* c, double out[6]);
 
 #ifdef __cplusplus
 }

@@ -1,6 +1,6 @@
 """Generate the golden fixtures in this directory from the reference's own backend.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_CHECKOUT
 
 Runs in the development container, where the reference source tree is mounted; the GPU box
 and the tests only read the committed .npz files.
@@ -121,7 +121,7 @@ def _program_json(prog):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of a basaltotech/bs-compiler checkout")
     args = ap.parse_args()
     ref = Path(args.reference)
     torch.set_num_threads(1)
