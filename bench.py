@@ -482,7 +482,10 @@ def run_basalto(args):
     else:
         owners = [partition(gshape[0], ws, r) for r in range(ws)]
         my_start, n_local = owners[rank]
-        G = slab_ghost_depth(prog, gshape, ws, dt)
+        transport = args.transport
+        if transport == "auto":  # peer stores for single-sweep passes; NCCL deep halos where sweeps fuse
+            transport = "nccl" if slab_ghost_depth(prog, gshape, ws, dt) > R[0] else "peer"
+        G = slab_ghost_depth(prog, gshape, ws, dt) if transport == "nccl" else R[0]
         local_shape = [n_local] + list(gshape[1:])
         plane = int(np.prod(gshape[1:]))
         x0 = torch.zeros([n_local + 2 * G] + list(gshape[1:]), dtype=w.dtype, device=dev)
@@ -502,11 +505,18 @@ def run_basalto(args):
         comm = h
         cp = prog.to_c(local_shape)
         shp = _abi.i64_array(local_shape)
+        sweep_fn = lib.bst_slab_sweeps_deep if transport == "nccl" else lib.bst_slab_sweeps_p2p
+
+        def register(buf):  # collective: every rank registers its buffers in the same order
+            if transport == "peer":
+                _abi.check(lib.bst_comm_register_slab(comm, ctypes.c_void_p(buf.data_ptr()), dt, plane, n_local, G))
+
+        register(a)
+        register(b)
 
         def slab_sweeps(src, dst, n):
-            _abi.check(lib.bst_slab_sweeps_deep(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
-                                                ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
-                                                n, sp))
+            _abi.check(sweep_fn(comm, ctypes.byref(cp), dt, len(local_shape), shp, G,
+                                ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()), n, sp))
 
         def step_on(src, pa, pb):
             slab_sweeps(src, pa, 1)          # sweep 1 reads the seeded slab, which stays unchanged
@@ -518,7 +528,7 @@ def run_basalto(args):
         def step():
             return step_on(x0, a, b)
 
-        kmax = max(1, G // R[0]) if R[0] else 1
+        kmax = max(1, G // R[0]) if R[0] and transport == "nccl" else 1
         slab_passes = 1 + len(fuse_plan(sweeps - 1, kmax))
         local_points = n_local * plane
         points_job = int(np.prod(gshape))
@@ -693,10 +703,20 @@ def run_basalto(args):
         ex_ms = statistics.median(times)
         nbrs = min(2, ws - 1)  # an interior rank's neighbours (an end rank's at N = 2)
         ex_bytes = 2 * nbrs * G * plane * es  # sent + received by that rank
-        halo = {"ghost_planes": G, "bytes_per_exchange": ex_bytes, "exchange_ms": round(ex_ms, 4),
-                "nvlink_gbs": round(ex_bytes / (ex_ms * 1e-3) / 1e9, 2), "exchanges_per_step": slab_passes,
-                "note": "one exchange timed on the device after a sleep kernel hides its host enqueue "
-                        "(median of 10, max over ranks); in the sweep loop it overlaps the interior launch"}
+        halo = {"transport": transport, "ghost_planes": G, "bytes_per_exchange": ex_bytes,
+                "nccl_exchange_ms": round(ex_ms, 4), "nccl_nvlink_gbs": round(ex_bytes / (ex_ms * 1e-3) / 1e9, 2),
+                "exchanges_per_step": slab_passes,
+                "note": "nccl_*: one NCCL exchange of the ghost planes timed alone on the device after a sleep kernel "
+                        "hides its host enqueue (median of 10, max over ranks)"}
+        if transport == "peer":
+            # the exchange rides inside the two boundary launches: their remote stores per pass
+            sent = nbrs * G * plane * es
+            bms = pass_times["boundary_ms"]
+            halo.update({"peer_bytes_stored_per_pass": sent, "boundary_launches_ms": bms,
+                         "peer_store_gbs": round(sent / (bms * 1e-3) / 1e9, 2) if bms > 0 else None,
+                         "peer_note": "per pass the boundary launches compute the first and last ghost-depth planes "
+                                      "and store them over NVLink into the neighbours' ghost planes; peer_store_gbs = "
+                                      "bytes stored remotely / boundary-launch time (compute included)"})
 
     # ---- e2e through the public API with host buffers ---------------------------------------
     e2e = None
@@ -764,6 +784,8 @@ def run_basalto(args):
         sx = [x0, torch.zeros_like(x0)]
         sa = [a, torch.zeros_like(a)]
         sb = [b, torch.zeros_like(b)]
+        register(sa[1])
+        register(sb[1])
         res = [None, None]
 
         def up(s):
@@ -810,7 +832,9 @@ def run_basalto(args):
             "vs_baseline": None, "dtype": _dtype_name(w), "data": "synthetic",
             "config": {"workload": w.label(),
                        "global_grid": "x".join(map(str, gshape)),
-                       "parallelism": (f"z-slab x{ws} ({scaling} scaling, {G} ghost planes per side)" if sharded
+                       "parallelism": (f"z-slab x{ws} ({scaling} scaling, {G} ghost planes per side, "
+                                       f"{'boundary planes stored into the neighbours over NVLink' if transport == 'peer' else 'NCCL ghost exchange'})"
+                                       if sharded
                                        else (f"{ws} independent replicas" if ws > 1 else "single GPU")),
                        "arithmetic": "fused multiply-add fold (BST_PROGRAM_CONTRACT)" if w.program.contract
                        else "separately rounded (bit-identical to eager torch)",
@@ -850,6 +874,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--transport", choices=["auto", "nccl", "peer"], default="auto",
+                    help="N > 1 ghost planes: peer = boundary launches store into the neighbours over NVLink "
+                         "(single-sweep passes); nccl = NCCL exchange (deep halos where sweeps fuse); auto = peer "
+                         "unless sweeps fuse")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

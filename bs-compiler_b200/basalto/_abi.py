@@ -98,6 +98,10 @@ SIGNATURES = [
     ("bst_slab_sweeps_deep", c_int32,
      [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
       c_void_p]),
+    ("bst_comm_register_slab", c_int32, [c_void_p, c_void_p, c_int32, c_int64, c_int64, c_int32]),
+    ("bst_slab_sweeps_p2p", c_int32,
+     [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
+      c_void_p]),
     ("bst_comm_profile_begin", c_int32, [c_void_p, c_int32]),
     ("bst_comm_profile_end", c_int32, [c_void_p, POINTER(c_double)]),
 ]

@@ -21,6 +21,12 @@ Deep halos: where a kernel fuses k sweeps per pass (temporal blocking), the ghos
 k x radius and the slab exchanges once per k sweeps instead of once per sweep; the depth
 defaults to what the library reports for the program (bst_slab_ghost_depth), capped by the
 smallest rank's owned planes.
+
+Peer transport (transport="peer", bst_slab_sweeps_p2p): no exchange step at all.  The two
+boundary launches of every sweep store their output planes both locally and, through CUDA IPC
+peer mappings over NVLink, straight into the neighbours' ghost planes, then raise a sequence
+flag in the neighbour's memory; the next sweep's boundary launches wait (bounded) for the
+neighbours' flags.  The interior launch runs meanwhile and never reads ghost planes.
 """
 from __future__ import annotations
 
@@ -143,9 +149,12 @@ class SlabDomain:
     """
 
     def __init__(self, program: StencilProgram, global_shape, dtype=torch.float32, device=None,
-                 timeout_s: float = 120.0, group=None, ghost: int | None = None):
+                 timeout_s: float = 120.0, group=None, ghost: int | None = None, transport: str = "nccl"):
         import torch.distributed as dist
 
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport is 'nccl' (exchange over NCCL) or 'peer' (boundary stores over NVLink)")
+        self.transport = transport
         if program.boundary != "zero" or program.ndim not in (2, 3) or program.ndim != len(global_shape):
             raise ValueError("slab sweeps need a same-size 2-D or 3-D program")
         self.program = program
@@ -155,7 +164,8 @@ class SlabDomain:
         gshape = tuple(int(s) for s in global_shape)
         self._dt = _abi.BST_F32 if dtype == torch.float32 else _abi.BST_F64
         if ghost is None:
-            ghost = slab_ghost_depth(program, gshape, ws, self._dt)
+            # peer transport sweeps one step per pass: ghosts as deep as the axis-0 radius
+            ghost = slab_ghost_depth(program, gshape, ws, self._dt) if transport == "nccl" else program.radius()[0]
         self.layout = SlabLayout(gshape, ws, rank, int(ghost))
         if self.layout.ghost < program.radius()[0]:
             raise ValueError("ghost depth is below the program's axis-0 radius")
@@ -177,6 +187,12 @@ class SlabDomain:
             _abi.check(_abi.lib().bst_comm_create(uid, ws, rank, self.device.index, float(timeout_s), ctypes.byref(h)))
         self._comm = h
         self.current = self.a
+        if transport == "peer":  # collective: every rank registers its two buffers in this order
+            for buf in (self.a, self.b):
+                with torch.cuda.device(self.device):
+                    _abi.check(_abi.lib().bst_comm_register_slab(self._comm, ctypes.c_void_p(buf.data_ptr()), self._dt,
+                                                                 self.layout.plane_elems, self.layout.n_local,
+                                                                 self.layout.ghost))
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -201,8 +217,9 @@ class SlabDomain:
         """nsteps sweeps; returns the buffer holding the result (ghosts valid)."""
         L = self.layout
         other = self.b if self.current is self.a else self.a
+        fn = _abi.lib().bst_slab_sweeps_deep if self.transport == "nccl" else _abi.lib().bst_slab_sweeps_p2p
         with torch.cuda.device(self.device):
-            _abi.check(_abi.lib().bst_slab_sweeps_deep(
+            _abi.check(fn(
                 self._comm, ctypes.byref(self._cprog), self._dt, len(L.local_shape), _abi.i64_array(L.local_shape),
                 L.ghost, ctypes.c_void_p(self.current.data_ptr()), ctypes.c_void_p(other.data_ptr()), int(nsteps),
                 self._stream()))

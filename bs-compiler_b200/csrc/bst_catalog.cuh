@@ -128,7 +128,7 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 #define BST_STAR_RB 2  // two planes per stage: half the per-group bookkeeping per plane
 #endif
 #ifndef BST_STAR_PAIR
-#define BST_STAR_PAIR 0  // fp32 points two at a time (paired add/mul)
+#define BST_STAR_PAIR 1  // fp32 points two at a time (paired add / fma instructions, exact)
 #endif
 template <typename T, class S>
 using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX, bool(BST_STAR_HALO_LDS),
@@ -230,6 +230,7 @@ bool tb_eligible(const LaunchReq& r) {
 
 template <typename T, class C>
 int launch_tb2d(const LaunchReq& r) {
+  if (int rc = peer_unsupported(r, "the temporally blocked kernel")) return rc;
   const Canon& c = *r.c;
   constexpr int E = sizeof(T);
   const long long nm = r.m_hi - r.m_lo;

@@ -128,7 +128,11 @@ int check_device_error(cudaStream_t st) {
   if (h != 0) {
     BST_CUDA(cudaMemsetAsync(w, 0, sizeof h, st));
     BST_CUDA(cudaStreamSynchronize(st));
-    return fail(BST_ERR_TIMEOUT, "a kernel gave up waiting for a TMA stage (error bits " + std::to_string(h) + ")");
+    std::string what;
+    if (h & 1u) what += "a TMA stage that never landed";
+    if (h & 2u) what += std::string(what.empty() ? "" : " and ") + "a neighbour's ghost planes that never arrived";
+    if (what.empty()) what = "an unknown wait";
+    return fail(BST_ERR_TIMEOUT, "a kernel gave up waiting for " + what + " (error bits " + std::to_string(h) + ")");
   }
   return BST_OK;
 }
@@ -235,9 +239,9 @@ struct LaunchReq;
 template <typename T>
 int dispatch_sweep(const LaunchReq& r);
 int dispatch_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st);
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
 int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st);
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
 int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
 int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
 int dispatch_tb_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
@@ -246,9 +250,9 @@ int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y,
                     int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
-                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st) {
-  if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st);
-  if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st);
+                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer) {
+  if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st, peer);
+  if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st, peer);
   return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
 }
 
@@ -471,6 +475,7 @@ int bst_device_caps_query(int32_t device, bst_device_caps* out) {
   int drv = 0;
   cudaDriverGetVersion(&drv);
   out->driver_version = drv;
+  fill_driver_string(out);
   return BST_OK;
 }
 

@@ -3,8 +3,9 @@
 
 namespace bst {
 int dispatch_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st) {
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer) {
   LaunchReq r{&c, x, {xs[0], xs[1], xs[2]}, y, {ys[0], ys[1], ys[2]}, m_lo, m_hi, st};
+  r.peer = peer;
   return dispatch_sweep<float>(r);
 }
 int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]) {

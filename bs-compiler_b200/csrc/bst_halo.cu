@@ -1,9 +1,13 @@
-// bst_halo.cu — Z-slab ghost-plane exchange over NCCL and the overlapped slab sweep.
+// bst_halo.cu — Z-slab ghost planes across GPUs: the NCCL exchange, the overlapped slab sweep,
+// and the peer-memory slab sweep whose boundary launches store straight into the neighbours'
+// ghost planes over NVLink.
 //
 // NCCL is bound at run time with dlopen (as crates/basalto-communication/src/nccl.rs:43-85
 // does), preferring the copy already loaded in the process (torch's), so a process never
 // mixes two NCCL builds.  Communicators are created non-blocking and polled with a host
 // timeout; on timeout they are aborted and an error is returned instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>  // types and enums only; every call goes through the dlopen'd table
@@ -17,6 +21,7 @@
 #include <vector>
 
 #include "bst_internal.h"
+#include "bst_kernels.cuh"
 
 namespace bst {
 
@@ -102,6 +107,30 @@ struct bst_comm {
   // boundary start/end, exchange start/end, interior start/end.
   std::vector<cudaEvent_t> prof;
   int prof_cap = 0, prof_used = 0;
+  // Peer-memory slabs (bst_comm_register_slab / bst_slab_sweeps_p2p).
+  struct PeerSlab {
+    char* local = nullptr;  // this rank's buffer (plane 0 = the first lower ghost plane)
+    int64_t n_local = 0, plane = 0;
+    int32_t ghost = 0, es = 0;
+    char* lo = nullptr;  // rank-1's buffer registered in the same slot (peer mapping), or null
+    char* hi = nullptr;  // rank+1's
+    int64_t n_lo = 0, n_hi = 0;  // their owned planes
+    int32_t g_lo = 0, g_hi = 0;  // their ghost depths
+  };
+  std::vector<PeerSlab> slabs;
+  // flags[0]: last pass whose planes rank-1 stored here; flags[1]: the same for rank+1;
+  // flags[2], flags[3]: completion counters of this rank's lower / upper boundary launches.
+  unsigned long long* flags = nullptr;
+  unsigned long long* flag_lo_remote = nullptr;  // rank-1's flags[1]
+  unsigned long long* flag_hi_remote = nullptr;  // rank+1's flags[0]
+  unsigned long long seq = 0;                     // peer passes issued so far
+  void* xfer = nullptr;                           // device staging for the setup messages
+  struct Mapping {
+    int peer;
+    cudaIpcMemHandle_t handle;
+    char* base;
+  };
+  std::vector<Mapping> mappings;  // opened peer allocations (closed on destroy)
 };
 
 namespace bst {
@@ -124,6 +153,148 @@ static int wait_comm(bst_comm* c, const char* what) {
     else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
+// Bounded wait (about 2 s) by one thread until the neighbours' flags reach v_lo / v_hi (a null
+// flag is not waited for); on expiry the error word gets kErrPeerTimeout and the wait ends.
+// Queued ahead of the boundary launches, which read the ghost planes the neighbours store here
+// and store into theirs.
+__global__ void wait_peer_kernel(const unsigned long long* f_lo, unsigned long long v_lo,
+                                 const unsigned long long* f_hi, unsigned long long v_hi, unsigned* err) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    unsigned long long a = ~0ull, b = ~0ull;
+    if (f_lo) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(f_lo) : "memory");
+    if (f_hi) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(b) : "l"(f_hi) : "memory");
+    if (a >= v_lo && b >= v_hi) return;
+    if (global_ns() - t0 > 2000000000ull) {
+      atomicOr(err, kErrPeerTimeout);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
+// Poll a stream until its work is done, bounded by the communicator's timeout (a neighbour that
+// never joins the NCCL group must not hang the caller).
+static int wait_stream_bounded(bst_comm* c, cudaStream_t st, const char* what) {
+  NcclApi& a = nccl();
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) return BST_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(e, what);
+    ncclResult_t st_nccl = ncclSuccess;
+    if (a.CommGetAsyncError(c->comm, &st_nccl) == ncclSuccess && st_nccl != ncclSuccess && st_nccl != ncclInProgress)
+      return nccl_fail(st_nccl, what);
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > c->timeout_s) return fail(BST_ERR_TIMEOUT, std::string(what) + ": timed out");
+    std::this_thread::sleep_for(std::chrono::microseconds(el < 2e-3 ? 5 : 100));
+  }
+}
+
+// What a rank tells its neighbours about one registered buffer.
+struct PeerMsg {
+  cudaIpcMemHandle_t handle;
+  uint64_t offset;   // the buffer's start inside that allocation
+  int64_t n_local;   // owned planes
+  int64_t plane;     // elements per plane
+  int32_t ghost;     // ghost planes per side
+  int32_t es;        // element size
+};
+static_assert(sizeof(PeerMsg) <= 256, "one staging slot per message");
+
+// Send `mine` to rank-1 and rank+1 and receive theirs (zeroed where there is no neighbour).
+static int swap_with_neighbours(bst_comm* c, const PeerMsg& mine, PeerMsg* from_lo, PeerMsg* from_hi) {
+  std::memset(from_lo, 0, sizeof *from_lo);
+  std::memset(from_hi, 0, sizeof *from_hi);
+  if (c->nranks == 1) return BST_OK;
+  char* x = static_cast<char*>(c->xfer);
+  BST_CUDA(cudaMemcpy(x, &mine, sizeof mine, cudaMemcpyHostToDevice));
+  NcclApi& a = nccl();
+  ncclResult_t r = a.GroupStart();
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGroupStart");
+  ncclResult_t e[4] = {ncclSuccess, ncclSuccess, ncclSuccess, ncclSuccess};
+  if (c->rank > 0) {
+    e[0] = a.Send(x, sizeof(PeerMsg), ncclUint8, c->rank - 1, c->comm, c->comm_stream);
+    e[1] = a.Recv(x + 256, sizeof(PeerMsg), ncclUint8, c->rank - 1, c->comm, c->comm_stream);
+  }
+  if (c->rank < c->nranks - 1) {
+    e[2] = a.Send(x, sizeof(PeerMsg), ncclUint8, c->rank + 1, c->comm, c->comm_stream);
+    e[3] = a.Recv(x + 512, sizeof(PeerMsg), ncclUint8, c->rank + 1, c->comm, c->comm_stream);
+  }
+  r = a.GroupEnd();
+  for (ncclResult_t v : e)
+    if (v != ncclSuccess && v != ncclInProgress) return nccl_fail(v, "ncclSend/ncclRecv (peer setup)");
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclGroupEnd (peer setup)");
+  int rc = wait_comm(c, "peer setup enqueue");
+  if (rc) return rc;
+  rc = wait_stream_bounded(c, c->comm_stream, "peer setup exchange");
+  if (rc) return rc;
+  if (c->rank > 0) BST_CUDA(cudaMemcpy(from_lo, x + 256, sizeof *from_lo, cudaMemcpyDeviceToHost));
+  if (c->rank < c->nranks - 1) BST_CUDA(cudaMemcpy(from_hi, x + 512, sizeof *from_hi, cudaMemcpyDeviceToHost));
+  return BST_OK;
+}
+
+// This rank's message for the allocation holding `p`.
+static int describe(const void* p, PeerMsg* m) {
+  static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (!range) return fail(BST_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS)
+    return fail(BST_ERR_INVALID, "the slab buffer is not CUDA device memory");
+  BST_CUDA(cudaIpcGetMemHandle(&m->handle, reinterpret_cast<void*>(base)));
+  m->offset = uint64_t(reinterpret_cast<uintptr_t>(p) - uintptr_t(base));
+  return BST_OK;
+}
+
+// The neighbour's buffer described by `m`, mapped into this process (each allocation once).
+static int map_peer(bst_comm* c, int peer, const PeerMsg& m, char** out) {
+  for (const auto& mp : c->mappings)
+    if (mp.peer == peer && std::memcmp(&mp.handle, &m.handle, sizeof m.handle) == 0) {
+      *out = mp.base + m.offset;
+      return BST_OK;
+    }
+  void* base = nullptr;
+  BST_CUDA(cudaIpcOpenMemHandle(&base, m.handle, cudaIpcMemLazyEnablePeerAccess));
+  c->mappings.push_back(bst_comm::Mapping{peer, m.handle, static_cast<char*>(base)});
+  *out = static_cast<char*>(base) + m.offset;
+  return BST_OK;
+}
+
+// First use: the flag words, exchanged with the neighbours like a slab.
+static int ensure_flags(bst_comm* c) {
+  if (c->flags) return BST_OK;
+  BST_CUDA(cudaMalloc(&c->xfer, 1024));
+  void* f = nullptr;
+  BST_CUDA(cudaMalloc(&f, 256));
+  BST_CUDA(cudaMemset(f, 0, 256));
+  c->flags = static_cast<unsigned long long*>(f);
+  PeerMsg mine{}, lo{}, hi{};
+  int rc = describe(c->flags, &mine);
+  if (rc) return rc;
+  rc = swap_with_neighbours(c, mine, &lo, &hi);
+  if (rc) return rc;
+  char* p = nullptr;
+  if (c->rank > 0) {
+    if ((rc = map_peer(c, c->rank - 1, lo, &p))) return rc;
+    c->flag_lo_remote = reinterpret_cast<unsigned long long*>(p) + 1;  // rank-1 hears from its upper neighbour
+  }
+  if (c->rank < c->nranks - 1) {
+    if ((rc = map_peer(c, c->rank + 1, hi, &p))) return rc;
+    c->flag_hi_remote = reinterpret_cast<unsigned long long*>(p) + 0;  // rank+1 hears from its lower neighbour
+  }
+  return BST_OK;
+}
+
 }  // namespace bst
 
 static void release_profile(bst_comm* c) {
@@ -139,8 +310,20 @@ static cudaError_t prof_mark(bst_comm* c, int which, cudaStream_t st) {
   return cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + which], st);
 }
 
+static void release_peers(bst_comm* c) {
+  for (auto& m : c->mappings) cudaIpcCloseMemHandle(m.base);
+  c->mappings.clear();
+  c->slabs.clear();
+  if (c->flags) cudaFree(c->flags);
+  if (c->xfer) cudaFree(c->xfer);
+  c->flags = nullptr;
+  c->xfer = nullptr;
+  c->flag_lo_remote = c->flag_hi_remote = nullptr;
+}
+
 static void release_cuda(bst_comm* c) {
   release_profile(c);
+  release_peers(c);
   if (c->ev_bnd) cudaEventDestroy(c->ev_bnd);
   if (c->ev_comm) cudaEventDestroy(c->ev_comm);
   for (cudaEvent_t& ev : c->ev_b)
@@ -475,6 +658,144 @@ int bst_comm_profile_end(bst_comm* c, double out[6]) {
   out[4] = double(c->prof_used);
   release_profile(c);
   return rc;
+}
+
+int bst_comm_register_slab(bst_comm* c, void* buf, int32_t dtype, int64_t plane_elems, int64_t n_local,
+                           int32_t ghost) {
+  clear_error();
+  if (!c || !buf) return fail(BST_ERR_INVALID, "null argument");
+  if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+  if (plane_elems <= 0 || n_local <= 0 || ghost < 0) return fail(BST_ERR_INVALID, "bad slab geometry");
+  BST_CUDA(cudaSetDevice(c->device));
+  int rc = ensure_flags(c);
+  if (rc) return rc;
+  PeerMsg mine{}, lo{}, hi{};
+  if ((rc = describe(buf, &mine))) return rc;
+  mine.n_local = n_local;
+  mine.plane = plane_elems;
+  mine.ghost = ghost;
+  mine.es = dtype == BST_F64 ? 8 : 4;
+  if ((rc = swap_with_neighbours(c, mine, &lo, &hi))) return rc;
+  bst_comm::PeerSlab ps;
+  ps.local = static_cast<char*>(buf);
+  ps.n_local = n_local;
+  ps.plane = plane_elems;
+  ps.ghost = ghost;
+  ps.es = mine.es;
+  for (int side = 0; side < 2; ++side) {
+    const bool has = side == 0 ? c->rank > 0 : c->rank < c->nranks - 1;
+    if (!has) continue;
+    const PeerMsg& m = side == 0 ? lo : hi;
+    if (m.plane != plane_elems || m.es != mine.es || m.ghost != ghost)
+      return fail(BST_ERR_INVALID, "neighbouring slabs registered in the same slot differ in plane size, dtype or "
+                                   "ghost depth (register the buffers in the same order on every rank)");
+    char* p = nullptr;
+    if ((rc = map_peer(c, side == 0 ? c->rank - 1 : c->rank + 1, m, &p))) return rc;
+    if (side == 0) {
+      ps.lo = p;
+      ps.n_lo = m.n_local;
+      ps.g_lo = m.ghost;
+    } else {
+      ps.hi = p;
+      ps.n_hi = m.n_local;
+      ps.g_hi = m.ghost;
+    }
+  }
+  c->slabs.push_back(ps);
+  return BST_OK;
+}
+
+int bst_slab_sweeps_p2p(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                        int32_t ghost, void* a, void* b, int32_t nsteps, void* stream) {
+  clear_error();
+  if (!c || !prog || !local_shape || !a || !b) return fail(BST_ERR_INVALID, "null argument");
+  if (a == b) return fail(BST_ERR_INVALID, "ping-pong slabs must differ");
+  if (nsteps < 0) return fail(BST_ERR_INVALID, "negative step count");
+  if (dtype != BST_F32 && dtype != BST_F64) return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
+  if (ndim < 2 || ndim > 3) return fail(BST_ERR_INVALID, "slabs split axis 0 of a 2-D or 3-D grid");
+  Canon k_canon;
+  int64_t s[3], plane = 0;
+  int rc = slab_canon(prog, ndim, local_shape, ghost, &k_canon, s, &plane);
+  if (rc) return rc;
+  const int R = k_canon.R[0];
+  const int64_t nl = local_shape[0];
+  const int64_t G = ghost;
+  if (ghost < R || ghost < 1) return fail(BST_ERR_INVALID, "ghost depth is below the program's axis-0 radius");
+  if (nl < 2 * G) return fail(BST_ERR_INVALID, "each rank must own at least 2 x ghost planes");
+  const size_t es = dtype == BST_F64 ? 8 : 4;
+  // Both buffers receive boundary planes from the neighbours, so both must be registered slabs.
+  const bst_comm::PeerSlab* reg[2] = {nullptr, nullptr};
+  void* bufs[2] = {a, b};
+  for (int i = 0; i < 2; ++i) {
+    for (const auto& ps : c->slabs)
+      if (ps.local == bufs[i] && ps.n_local == nl && ps.plane == plane && ps.ghost == ghost && size_t(ps.es) == es)
+        reg[i] = &ps;
+    const bool written = i == 1 ? nsteps >= 1 : nsteps >= 2;  // pass k writes bufs[(k + 1) % 2]
+    if (!reg[i] && c->nranks > 1 && written)
+      return fail(BST_ERR_INVALID, "bst_slab_sweeps_p2p: every buffer it writes must be registered with "
+                                   "bst_comm_register_slab (same geometry)");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  BST_CUDA(cudaSetDevice(c->device));
+  unsigned* err = device_error_word();
+  if (!err) return fail(BST_ERR_CUDA, "device error word unavailable");
+  const size_t ghost_bytes = size_t(G) * plane * es;
+  int cur = 0;  // index of src in bufs
+  BST_CUDA(cudaEventRecord(c->ev_int, st));
+  for (int k = 0; k < nsteps; ++k) {
+    char* src = static_cast<char*>(bufs[cur]);
+    char* dst = static_cast<char*>(bufs[1 - cur]);
+    const bst_comm::PeerSlab* dreg = reg[1 - cur];
+    void* out = dst + ghost_bytes;
+    const unsigned long long seq = ++c->seq;
+    BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
+    const bool lo = c->nranks > 1 && c->rank > 0, hi = c->nranks > 1 && c->rank < c->nranks - 1;
+    if (lo || hi) {
+      // The neighbours' previous pass has stored this pass's input ghosts here and is done
+      // reading the ghost planes this pass stores into.
+      wait_peer_kernel<<<1, 32, 0, c->bnd_stream>>>(lo ? c->flags + 0 : nullptr, seq - 1,
+                                                     hi ? c->flags + 1 : nullptr, seq - 1, err);
+      BST_CUDA(cudaGetLastError());
+    }
+    BST_CUDA(prof_mark(c, 0, c->bnd_stream));
+    PeerStore p_lo{}, p_hi{};
+    if (lo) {
+      // owned plane m (< G) -> rank-1's upper ghost plane g_lo + n_lo + m
+      p_lo.delta_bytes = (long long)(intptr_t(dreg->lo) - intptr_t(dst)) +
+                         (long long)(dreg->g_lo + dreg->n_lo - G) * (long long)(plane * es);
+      p_lo.done_count = c->flags + 2;
+      p_lo.flag = c->flag_lo_remote;
+      p_lo.seq = seq;
+    }
+    if (hi) {
+      // owned plane m (>= nl - G) -> rank+1's lower ghost plane m - (nl - G)
+      p_hi.delta_bytes = (long long)(intptr_t(dreg->hi) - intptr_t(dst)) - (long long)nl * (long long)(plane * es);
+      p_hi.done_count = c->flags + 3;
+      p_hi.flag = c->flag_hi_remote;
+      p_hi.seq = seq;
+    }
+    rc = launch_sweep(k_canon, dtype, src, s, out, s, 0, G, c->bnd_stream, lo ? &p_lo : nullptr);
+    if (!rc) rc = launch_sweep(k_canon, dtype, src, s, out, s, nl - G, nl, c->bnd_stream, hi ? &p_hi : nullptr);
+    if (rc) return rc;
+    BST_CUDA(prof_mark(c, 1, c->bnd_stream));
+    BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+    if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
+    BST_CUDA(prof_mark(c, 4, st));
+    if (G < nl - G) {
+      rc = launch_sweep(k_canon, dtype, src, s, out, s, G, nl - G, st);
+      if (rc) return rc;
+    }
+    BST_CUDA(prof_mark(c, 5, st));
+    if (c->prof_used < c->prof_cap) {  // the exchange rides inside the boundary launches
+      BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 2], c->bnd_stream));
+      BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 3], c->bnd_stream));
+      ++c->prof_used;
+    }
+    BST_CUDA(cudaEventRecord(c->ev_int, st));
+    cur = 1 - cur;
+  }
+  if (nsteps > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(nsteps - 1) % 2], 0));
+  return BST_OK;
 }
 
 int bst_slab_sweeps(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,

@@ -261,7 +261,7 @@ static int parse_dtype(const char* s) {
   return -1;
 }
 
-static void fill_driver_string(bst_device_caps* c) {
+void fill_driver_string(bst_device_caps* c) {
   std::snprintf(c->vendor, sizeof c->vendor, "%s", "nvidia");
   std::snprintf(c->driver, sizeof c->driver, "%s", "unknown");
   std::ifstream f("/proc/driver/nvidia/version");

@@ -47,10 +47,11 @@ int canonicalize(const bst_program* p, int ndim, const int64_t* shape, Canon* c)
 // Logical strides [M, Y, X] from torch-order strides (elements).
 void logical_strides(int ndim, const int64_t* strides, int64_t out[3]);
 
-// Launch one sweep.  x/y strides are logical [M,Y,X]; m range is in output planes.
-// `slab_ghost` > 0 marks an input whose axis-0 ghosts are physically present.
+// Launch one sweep.  x/y strides are logical [M,Y,X]; m range is in output planes.  `peer`:
+// also store every output into a neighbouring GPU's memory (TMA march kernels only).
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
-                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st);
+                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st,
+                 const PeerStore* peer = nullptr);
 
 // Temporal blocking.  tb_max_sweeps: most sweeps one launch can fuse for this request
 // (1 = no fused kernel).  launch_fused: k sweeps of output planes [m_lo, m_hi) in one launch
@@ -75,6 +76,10 @@ Schedule march_schedule();
 // when the cache is full or the upload failed (the caller then uploads for one call).
 constexpr int kTableCacheMax = 256;
 const void* cached_device_table(const void* blob, size_t bytes);
+
+// vendor ("nvidia") and driver (the NVRM version field of /proc/driver/nvidia/version, as
+// crates/basalto-common/src/hardware.rs:154-159 reads it; "unknown" without it).
+void fill_driver_string(bst_device_caps* c);
 
 // Device error word (kernels OR bits into it); allocated once per device.
 unsigned* device_error_word();

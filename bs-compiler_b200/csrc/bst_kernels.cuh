@@ -25,7 +25,7 @@
 namespace bst {
 
 // Error word bits written by kernels (host reads them back on request).
-enum : unsigned { kErrTmaTimeout = 1u };
+enum : unsigned { kErrTmaTimeout = 1u, kErrPeerTimeout = 2u };
 
 constexpr int round_up_c(int v, int m) { return (v + m - 1) / m * m; }
 constexpr int floor_div_c(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
@@ -270,6 +270,7 @@ struct MarchArgs {
   int balanced;
   unsigned* err;
   int vec_store;  // output rows are 16-byte aligned and contiguous in x
+  PeerStore peer;  // optional second destination on a neighbouring GPU (slab boundary planes)
 };
 
 // Balanced contiguous range of CTA b among G CTAs over W units.
@@ -400,6 +401,7 @@ __device__ __forceinline__ EvalCoefs<T, C> eval_coefs(const Coefs<T, C::shape::N
 #pragma unroll
     for (int g = 0; g < C::shape::NTERMS; ++g) p.scale[g] = make_float2(c.scale[g], c.scale[g]);
     p.init_zero = c.init_zero;
+    p.negzero = make_float2(c.negzero, c.negzero);
     return p;
   } else {
     return c;
@@ -425,30 +427,42 @@ __device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const EvalCoe
   }
 }
 
+// One row of VX outputs to `d` and, when pd != 0, also to the same position pd bytes away (a
+// neighbouring GPU's ghost planes, through its peer mapping).  `interior`: the whole tile is
+// inside the output and rows are 16-byte aligned (unchecked vector stores).
+template <typename T, class C>
+__device__ __forceinline__ void store_row(T* d, const T (&res)[C::VX], bool interior, bool row_ok, int cols_left,
+                                          long long so2, long long pd) {
+  using VT = typename Vec16<T>::type;
+  if (interior) {
+    VT q;
+    T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+    for (int v = 0; v < C::VX; ++v) e[v] = res[v];
+    *reinterpret_cast<VT*>(d) = q;
+    if (pd) *reinterpret_cast<VT*>(reinterpret_cast<char*>(d) + pd) = q;
+  } else if (row_ok) {
+#pragma unroll
+    for (int v = 0; v < C::VX; ++v)
+      if (v < cols_left) {
+        d[v * so2] = res[v];
+        if (pd) *reinterpret_cast<T*>(reinterpret_cast<char*>(d + v * so2) + pd) = res[v];
+      }
+  }
+}
+
 // Evaluate the PY x VX points of one plane step and store them.  `dst` points at the
-// thread's first output of row 0 of this plane; `interior` = the whole tile is inside the
-// output and rows are 16-byte aligned (unchecked vector stores).
+// thread's first output of row 0 of this plane.
 template <typename T, class C, int P, int... Js>
 __device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                            T* __restrict__ dst, long long so1, bool interior, int rows_left,
-                                           int cols_left, long long so2, std::integer_sequence<int, Js...>) {
-  using VT = typename Vec16<T>::type;
+                                           int cols_left, long long so2, long long pd,
+                                           std::integer_sequence<int, Js...>) {
   (
       [&] {
         T res[C::VX];
         eval_row<T, C, P, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
-        T* d = dst + Js * so1;
-        if (interior) {
-          VT q;
-          T* e = reinterpret_cast<T*>(&q);
-#pragma unroll
-          for (int v = 0; v < C::VX; ++v) e[v] = res[v];
-          *reinterpret_cast<VT*>(d) = q;
-        } else if (Js < rows_left) {
-#pragma unroll
-          for (int v = 0; v < C::VX; ++v)
-            if (v < cols_left) d[v * so2] = res[v];
-        }
+        store_row<T, C>(dst + Js * so1, res, interior, Js < rows_left, cols_left, so2, pd);
       }(),
       ...);
 }
@@ -527,25 +541,9 @@ __device__ __forceinline__ void stream_fill(MarchRegs<T, C>& r, const T* const* 
 // Store the PY x VX completed points of slot 0 (same rules as eval_store).
 template <typename T, class C, int... Js>
 __device__ __forceinline__ void stream_store(const MarchRegs<T, C>& r, T* __restrict__ dst, long long so1,
-                                             bool interior, int rows_left, int cols_left, long long so2,
+                                             bool interior, int rows_left, int cols_left, long long so2, long long pd,
                                              std::integer_sequence<int, Js...>) {
-  using VT = typename Vec16<T>::type;
-  (
-      [&] {
-        T* d = dst + Js * so1;
-        if (interior) {
-          VT q;
-          T* e = reinterpret_cast<T*>(&q);
-#pragma unroll
-          for (int v = 0; v < C::VX; ++v) e[v] = r.acc[0][Js][v];
-          *reinterpret_cast<VT*>(d) = q;
-        } else if (Js < rows_left) {
-#pragma unroll
-          for (int v = 0; v < C::VX; ++v)
-            if (v < cols_left) d[v * so2] = r.acc[0][Js][v];
-        }
-      }(),
-      ...);
+  (store_row<T, C>(dst + Js * so1, r.acc[0][Js], interior, Js < rows_left, cols_left, so2, pd), ...);
 }
 
 // One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store (the window
@@ -553,11 +551,11 @@ __device__ __forceinline__ void stream_store(const MarchRegs<T, C>& r, T* __rest
 template <typename T, class C, int P>
 __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                            const EvalCoefs<T, C>& coef, T* dst, long long so1,
-                                           bool interior, int rows_left, int cols_left, long long so2) {
+                                           bool interior, int rows_left, int cols_left, long long so2, long long pd) {
   if constexpr (C::STREAM) {
     stream_rows<T, C, P + 2 * C::RM>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
     stream_apply<T, C>(r, coef, std::make_integer_sequence<int, 2 * C::RM + 1>{});
-    stream_store<T, C>(r, dst, so1, interior, rows_left, cols_left, so2, std::make_integer_sequence<int, C::PY>{});
+    stream_store<T, C>(r, dst, so1, interior, rows_left, cols_left, so2, pd, std::make_integer_sequence<int, C::PY>{});
 #pragma unroll
     for (int k = 0; k < 2 * C::RM; ++k)
 #pragma unroll
@@ -572,7 +570,7 @@ __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* s
     }
     if constexpr (C::NSEG > 0)
       load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
-    eval_store<T, C, P>(r, coef, dst, so1, interior, rows_left, cols_left, so2,
+    eval_store<T, C, P>(r, coef, dst, so1, interior, rows_left, cols_left, so2, pd,
                         std::make_integer_sequence<int, C::PY>{});
   }
 }
@@ -581,10 +579,11 @@ template <typename T, class C, int... Ps>
 __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                             const EvalCoefs<T, C>& coef, T* dst0, long long so0,
                                             long long so1, bool interior, int rows_left, int cols_left,
-                                            long long so2, int planes, std::integer_sequence<int, Ps...>) {
+                                            long long so2, long long pd, int planes,
+                                            std::integer_sequence<int, Ps...>) {
   // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
   ((Ps < planes ? plane_step<T, C, Ps>(r, sb, toff, lane_x, coef, dst0 + Ps * so0, so1, interior, rows_left,
-                                       cols_left, so2)
+                                       cols_left, so2, pd)
                 : void()),
    ...);
   if constexpr (C::WINDOW) {  // next group: its planes g0+RB-WM .. are slots RB ..
@@ -594,6 +593,22 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
       for (int j = 0; j < C::PY; ++j)
 #pragma unroll
         for (int e = 0; e < C::VX; ++e) r.win[k][j][e] = r.win[k + C::RB][j][e];
+  }
+}
+
+// End of a launch that stored into a neighbour's ghost planes: every thread's stores are made
+// visible system-wide, and the CTA that finishes last sets the neighbour's sequence flag to
+// peer.seq (it reads that flag before its next pass touches those planes).
+__device__ __forceinline__ void peer_signal(const PeerStore& p) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long done = atomicAdd(p.done_count, 1ull) + 1ull;
+    if (done == gridDim.x) {
+      *p.done_count = 0ull;  // every CTA has counted: reset for the next launch
+      __threadfence_system();
+      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.flag), "l"(p.seq) : "memory");
+    }
   }
 }
 
@@ -730,7 +745,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
       const long long m_grp = (long long)grp * C::RB;
       const int planes = int(me - mb - m_grp);
       group_steps<T, C>(r, sb, toff, lane_x, ecoef, out_item + m_grp * g.so[0], g.so[0], g.so[1], interior,
-                        rows_left, cols_left, g.so[2], planes, std::make_integer_sequence<int, C::RB>{});
+                        rows_left, cols_left, g.so[2], a.peer.delta_bytes, planes,
+                        std::make_integer_sequence<int, C::RB>{});
     }
     if (failed) break;
     q_base += unsigned(qt);
@@ -750,6 +766,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     }
     __syncthreads();
   }
+  if (a.peer.flag) peer_signal(a.peer);  // (also after a failure, so the neighbour does not wait it out)
 }
 
 // ---------------------------------------------------------------------------------

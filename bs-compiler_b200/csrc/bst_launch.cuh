@@ -22,13 +22,22 @@ struct LaunchReq {
   // Temporally blocked launches: rows (output coordinates) whose intermediate levels are
   // computed; outside it they are ghost cells.  Default: the grid's own rows.
   int64_t row_lo = 0, row_hi = -1;
+  // Slab boundary launches: also store into a neighbouring GPU's ghost planes (TMA march only).
+  const PeerStore* peer = nullptr;
 };
+
+inline int peer_unsupported(const LaunchReq& r, const char* kernel) {
+  if (!r.peer) return BST_OK;
+  return fail(BST_ERR_UNSUPPORTED, std::string("peer-memory boundary stores need the TMA march kernel; this request "
+                                               "runs ") + kernel);
+}
 
 template <typename T, int N>
 Coefs<T, N> make_coefs(const Canon& c) {
   Coefs<T, N> k{};
   for (int g = 0; g < c.nterms && g < N; ++g) k.scale[g] = T(c.scale[g]);
   k.init_zero = c.init_zero;
+  k.negzero = T(-0.0);
   return k;
 }
 
@@ -52,6 +61,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // ---- direct ---------------------------------------------------------------------
 template <typename T, class S>
 int launch_direct(const LaunchReq& r) {
+  if (int rc = peer_unsupported(r, "the direct kernel")) return rc;
   const GridDesc g = make_grid(r);
   const long long total = (r.m_hi - r.m_lo) * g.no[1] * g.no[2];
   if (total <= 0) return BST_OK;
@@ -67,6 +77,7 @@ int launch_direct(const LaunchReq& r) {
 
 template <typename T>
 int launch_direct_table(const LaunchReq& r) {
+  if (int rc = peer_unsupported(r, "the runtime-table kernel")) return rc;
   const Canon& c = *r.c;
   const GridDesc g = make_grid(r);
   const long long total = (r.m_hi - r.m_lo) * g.no[1] * g.no[2];
@@ -126,6 +137,7 @@ int launch_direct_table(const LaunchReq& r) {
 // ---- 1-D line ---------------------------------------------------------------------
 template <typename T, class S, int ORG>
 int launch_line(const LaunchReq& r) {
+  if (int rc = peer_unsupported(r, "the 1-D line kernel")) return rc;
   constexpr int V = Vec16<T>::N;
   LineArgs a{r.c->n[2], r.c->no[2]};
   const long long nvec = (a.n_out + V - 1) / V;
@@ -308,6 +320,10 @@ int launch_march(const LaunchReq& r) {
                  (r.ys[0] * E) % 16 == 0)
                     ? 1
                     : 0;
+  if (r.peer) {
+    a.peer = *r.peer;
+    if (a.peer.delta_bytes % 16 != 0) a.vec_store = 0;  // the remote rows must be 16-byte aligned too
+  }
   dim3 block(C::THREADS);
   kern<<<unsigned(grid), block, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
                                                   make_coefs<T, C::shape::NTERMS>(c));

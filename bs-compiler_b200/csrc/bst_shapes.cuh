@@ -167,7 +167,7 @@ __device__ __forceinline__ T eval_term(const F& f, const Coefs<T, S::NTERMS>& c)
   constexpr int cnt = S::tbl.terms[G].count;
   T s = term_sum<S, G, T>(f, std::make_integer_sequence<int, cnt - 1>{});
   constexpr int op = S::tbl.terms[G].op;
-  if constexpr (op == kMul) return mul_rn(c.scale[G], s);
+  if constexpr (op == kMul) return product_rn(c.scale[G], s, c.negzero);
   else if constexpr (op == kDiv) return div_rn(s, c.scale[G]);
   else return s;
 }

@@ -34,12 +34,24 @@ struct GridDesc {
   int64_t m_lo, m_hi;  // output M range computed by this launch
 };
 
+// A second destination for a launch's stores on a neighbouring GPU (Z-slab boundary planes
+// written straight into the neighbour's ghost planes).  delta_bytes: address of the remote copy
+// minus the local output address (0 = none).  When the launch ends, the last CTA sets *flag
+// (the neighbour's memory) to seq; done_count is a zeroed local counter for that election.
+struct PeerStore {
+  long long delta_bytes;
+  unsigned long long* done_count;
+  unsigned long long* flag;
+  unsigned long long seq;
+};
+
 // Runtime scalars of a program (compile-time structure lives in the shape type);
 // passed by value, sized exactly to the shape's term count.
 template <typename T, int N>
 struct Coefs {
   T scale[N];
   int init_zero;
+  T negzero;  // -0.0, passed from the host so the compiler cannot fold it (product_rn)
 };
 
 // Runtime-table program for the generic kernels (lives in device memory).
@@ -68,16 +80,24 @@ __device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(
 __device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
 __device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
 
-// Two fp32 lanes per instruction (sm_100 paired add/mul/fma .f32x2).  CUDA documents each
-// component of __fadd2_rn / __fmul2_rn / __ffma2_rn as numerically identical to the scalar
-// __fadd_rn / __fmul_rn / __fmaf_rn, so a pair of points evaluated together rounds exactly as
-// two points evaluated apart.  There is no paired divide: its components divide separately.
+// Two fp32 lanes per instruction (sm_100 paired add/fma .f32x2).  One paired add or fma rounds
+// each component exactly as the scalar __fadd_rn / __fmaf_rn (checked on B200 over 2^24
+// components, special values included).  A paired multiply, however, is fused by the compiler
+// into a following paired add even when written with an explicit rounding mode, so products
+// are formed as fma(a, b, -0.0) instead (product_rn): that is exactly round(a*b) for every
+// input (a*b + (-0) == a*b, and +0 + -0 == +0), and an fma result cannot be fused further.
+// The -0.0 arrives as a kernel argument, so the compiler cannot fold the fma back into a
+// multiply.  There is no paired divide: its components divide separately.
 __device__ __forceinline__ float2 add_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 mul_rn(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 div_rn(float2 a, float2 b) {
   return make_float2(__fdiv_rn(a.x, b.x), __fdiv_rn(a.y, b.y));
 }
 __device__ __forceinline__ float2 fma_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// scale * s rounded once and kept apart from any later addition.
+__device__ __forceinline__ float product_rn(float a, float b, float) { return mul_rn(a, b); }
+__device__ __forceinline__ double product_rn(double a, double b, double) { return mul_rn(a, b); }
+__device__ __forceinline__ float2 product_rn(float2 a, float2 b, float2 negzero) { return __ffma2_rn(a, b, negzero); }
 
 template <typename T>
 __device__ __forceinline__ T zero_of() {

@@ -258,6 +258,34 @@ BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t d
                                  const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
                                  void* stream);
 
+/* ---- peer-memory slabs: the ghost exchange fused into the boundary sweep ----------
+ * bst_comm_register_slab registers one slab buffer ([ghost][n_local][ghost] planes of
+ * plane_elems elements along axis 0) for peer stores.  It is collective: every rank calls it
+ * for its own buffer, in the same order, so that slot i on one rank and slot i on its
+ * neighbours name the same logical buffer; neighbours then map each other's slot-i buffers over
+ * NVLink (CUDA IPC).  The buffer must be CUDA device memory that stays allocated while the
+ * communicator lives.  (The reference exchanges through NCCL or host staging before each
+ * launch, crates/basalto-communication/src/halo_exchange.rs:93-322.)
+ *
+ * bst_slab_sweeps_p2p: nsteps sweeps over (a, b) like bst_slab_sweeps, without NCCL in the
+ * loop.  Per sweep, the two boundary launches (the first and last `ghost` owned planes) store
+ * every output both into this rank's buffer and, through the peer mapping, into the
+ * neighbours' ghost planes; the last CTA of each boundary launch then sets the neighbour's
+ * sequence flag.  The next sweep's boundary launches start after a one-thread wait (bounded,
+ * about 2 s; a timeout sets the error bit bst_device_error_check reports) for both neighbours'
+ * flags.  The interior launch on `stream` runs concurrently and reads no ghost planes.
+ * Every buffer a sweep writes (b, and a when nsteps >= 2) must be registered with this
+ * geometry; a's ghost planes must hold the neighbours' planes of the input (for example after
+ * bst_halo_exchange).  Each rank must own at least 2 x ghost planes; ghost >= the axis-0
+ * radius; the program must run on the TMA march kernel (2-D/3-D catalog shapes).  Result in b
+ * when nsteps is odd, in a when even, ghosts complete.  All ranks must issue the same
+ * sequence of these calls. */
+BST_API int bst_comm_register_slab(bst_comm* c, void* buf, int32_t dtype, int64_t plane_elems, int64_t n_local,
+                                   int32_t ghost);
+BST_API int bst_slab_sweeps_p2p(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                                const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
+                                void* stream);
+
 /* Per-pass timing of the slab sweeps (diagnostics).  After bst_comm_profile_begin, the next
  * max_passes passes of bst_slab_sweeps_deep on this communicator record CUDA timing events
  * around their boundary launches, their ghost exchange and their interior launch.

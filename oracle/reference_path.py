@@ -39,4 +39,8 @@ def reference_backend(gm, example_inputs):
 
 
 def compile_reference(fn):
-    return torch.compile(fn, backend=reference_backend)
+    """fn compiled through the reference backend for one static shape (dynamic=False), so a
+    process that already compiled fn for another grid does not hand the backend symbolic
+    sizes."""
+    torch._dynamo.reset()
+    return torch.compile(fn, backend=reference_backend, dynamic=False)

@@ -84,7 +84,7 @@ def test_single_rank_deep_slab(dtype, shape, steps, ghost):
     nl = shape[0]
     per = 0
     for k in plan:
-        gx = max(plan)
+        gx = G  # every pass refreshes the full ghost depth
         lo_end = min(gx, nl)
         hi_begin = max(nl - gx, lo_end)
         per += 1 + (hi_begin < nl) + (lo_end < hi_begin)
@@ -102,7 +102,17 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, q):
+def _peer_programs():
+    """Shapes whose every rank owns at least 2 x radius planes at 4 ranks (peer transport)."""
+    from basalto import program as P
+    from basalto import workloads as W
+    return [(P.heat7_3d(), (37, 20, 64), torch.float32, 4),
+            (P.star_3d(P.LAPLACIAN8_COEFFS), (41, 24, 128), torch.float32, 3),
+            (P.box(3, 1, W.box27_weights()), (19, 16, 64), torch.float64, 3),
+            (P.jacobi5_2d(), (70, 256), torch.float32, 5)]
+
+
+def _rank(rank, world, port, q, transport="nccl"):
     import datetime
 
     import torch.distributed as dist
@@ -112,9 +122,9 @@ def _rank(rank, world, port, q):
     try:
         from basalto.slab import SlabDomain
         res = []
-        for prog, shape, dtype, steps in _programs():
+        for prog, shape, dtype, steps in (_programs() if transport == "nccl" else _peer_programs()):
             x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(41))
-            dom = SlabDomain(prog, shape, dtype=dtype, device=f"cuda:{rank}", timeout_s=60.0)
+            dom = SlabDomain(prog, shape, dtype=dtype, device=f"cuda:{rank}", timeout_s=60.0, transport=transport)
             try:
                 dom.load(x)
                 dom.run(steps)
@@ -128,22 +138,20 @@ def _rank(rank, world, port, q):
                 got = np.concatenate(parts, 0)
                 ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
                 res.append(bool(np.array_equal(got, ref)))
+        import basalto
+        basalto.check_device_errors(rank)  # no bounded wait (TMA stage or neighbour flag) gave up
         if rank == 0:
             q.put(res)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ranks_nccl_exchange_equals_single_grid(world):
-    """2 ranks: both global ends; 4 ranks: middle ranks with two neighbours as well."""
-    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
+def _spawn(world, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q, transport)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -153,5 +161,42 @@ def test_ranks_nccl_exchange_equals_single_grid(world):
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
+    return res, procs
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks_nccl_exchange_equals_single_grid(world):
+    """2 ranks: both global ends; 4 ranks: middle ranks with two neighbours as well."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res, procs = _spawn(world, "nccl")
     assert res == [True] * len(_programs())
     assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks_peer_stores_equal_single_grid(world):
+    """Boundary launches store into the neighbours' ghost planes over NVLink (no exchange
+    step); the gathered result equals the single-grid oracle bit for bit, and no bounded wait
+    for a neighbour's flag expired."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res, procs = _spawn(world, "peer")
+    assert res == [True] * len(_peer_programs())
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def test_single_rank_peer_transport_equals_single_grid():
+    """One rank: the peer path (no neighbours) is the boundary/interior split alone."""
+    from basalto.slab import SlabDomain
+    for prog, shape, dtype, steps in _peer_programs():
+        x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(8))
+        dom = SlabDomain(prog, shape, dtype=dtype, device="cuda:0", transport="peer")
+        try:
+            dom.load(x)
+            dom.run(steps)
+            got = dom.owned().cpu().numpy()
+        finally:
+            dom.close()
+        ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
+        assert np.array_equal(got, ref)
