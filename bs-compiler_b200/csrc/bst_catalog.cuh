@@ -130,9 +130,12 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 #ifndef BST_STAR_PAIR
 #define BST_STAR_PAIR 1  // fp32 points two at a time (paired add / fma instructions, exact)
 #endif
+#ifndef BST_STAR_MINB
+#define BST_STAR_MINB 1  // CTAs per SM the register allocation must allow
+#endif
 template <typename T, class S>
 using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX, bool(BST_STAR_HALO_LDS),
-                         false, bool(BST_STAR_WINDOW), 1, bool(BST_STAR_PAIR)>;
+                         false, bool(BST_STAR_WINDOW), BST_STAR_MINB, bool(BST_STAR_PAIR)>;
 // Boxes in ascending order stream: each input plane is applied to every output it touches as
 // it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
 #ifndef BST_BOXS_TY
@@ -153,9 +156,12 @@ using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_R
 #ifndef BST_BOXS_MINB
 #define BST_BOXS_MINB 2  // 2 CTAs per SM: the fused fold would otherwise take 76 registers
 #endif
+#ifndef BST_BOXS_PAIR
+#define BST_BOXS_PAIR 0  // fp32 points two at a time (paired add / fma instructions, exact)
+#endif
 template <typename T, class S>
 using CfgBoxS = MarchCfg<T, S, kRowCols<T>, BST_BOXS_TY, BST_BOXS_PY, BST_BOXS_RB, BST_BOXS_NSX, bool(BST_BOX_HALO_LDS),
-                         bool(BST_BOX_STREAM), true, BST_BOXS_MINB>;
+                         bool(BST_BOX_STREAM), true, BST_BOXS_MINB, bool(BST_BOXS_PAIR)>;
 
 // Whether BST_PROGRAM_CONTRACT changes this program's arithmetic: some multiplied term after
 // the first (only those fold as fma).

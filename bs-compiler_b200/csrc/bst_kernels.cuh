@@ -222,8 +222,8 @@ struct MarchCfg {
   // Window slots: a group of RB plane steps reads planes g0-WM .. g0+RB-1+WM (g0 = the group's
   // first output plane), so the window holds 2WM+RB planes and shifts by RB once per group.
   static constexpr int WSLOTS = WINDOW ? 2 * WM + RB : 1;
-  // fp32 points evaluated two at a time with paired instructions (gather mode only).
-  static constexpr bool PAIR = PAIR_ && sizeof(T) == 4 && !STREAM;
+  // fp32 points evaluated two at a time with paired instructions.
+  static constexpr bool PAIR = PAIR_ && sizeof(T) == 4;
   // Stages read by group g (input planes g*RB + [0, RB-1+2RM] relative to the item's first
   // loaded plane): the window keeps planes behind the current one in registers, so in window
   // mode group g only reads from plane g*RB + RM on and earlier stages retire early.
@@ -483,35 +483,54 @@ __device__ __forceinline__ void load_segments_at(MarchRegs<T, C>& r, const T* co
 // Offset DM's terms for point (J, V) of accumulator slot K; START: DM = -RM, the fold begins
 // (term 0, then the zero-start rule, exactly as eval_shape).
 template <typename T, class C, int DM, bool START, int K, int J, int V>
-__device__ __forceinline__ void stream_point(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c) {
+__device__ __forceinline__ void stream_point(MarchRegs<T, C>& r, const EvalCoefs<T, C>& c) {
   using S = typename C::shape;
   constexpr int gb = group_begin<S>(DM), ge = group_begin<S>(DM + 1);
-  const PointFetch<T, C, J, V> f{r};
-  if constexpr (START) {
-    static_assert(gb == 0 && ge >= 1, "the fold starts with offset -RM");
-    T acc = eval_term<S, 0, T>(f, c);
-    if (c.init_zero) acc = add_rn(T(0), acc);
-    r.acc[K][J][V] = fold_range<S, T, 1>(acc, f, c, std::make_integer_sequence<int, ge - 1>{});
+  if constexpr (C::PAIR) {  // points V and V + 1 in one pair (V even)
+    const PairFetch<C, J, V, 0> f{r};
+    float2 acc;
+    if constexpr (START) {
+      static_assert(gb == 0 && ge >= 1, "the fold starts with offset -RM");
+      acc = eval_term<S, 0, float2>(f, c);
+      if (c.init_zero) acc = add_rn(zero_of<float2>(), acc);
+      acc = fold_range<S, float2, 1>(acc, f, c, std::make_integer_sequence<int, ge - 1>{});
+    } else {
+      acc = fold_range<S, float2, gb>(make_float2(r.acc[K][J][V], r.acc[K][J][V + 1]), f, c,
+                                      std::make_integer_sequence<int, ge - gb>{});
+    }
+    r.acc[K][J][V] = acc.x;
+    r.acc[K][J][V + 1] = acc.y;
   } else {
-    r.acc[K][J][V] = fold_range<S, T, gb>(r.acc[K][J][V], f, c, std::make_integer_sequence<int, ge - gb>{});
+    const PointFetch<T, C, J, V> f{r};
+    if constexpr (START) {
+      static_assert(gb == 0 && ge >= 1, "the fold starts with offset -RM");
+      T acc = eval_term<S, 0, T>(f, c);
+      if (c.init_zero) acc = add_rn(T(0), acc);
+      r.acc[K][J][V] = fold_range<S, T, 1>(acc, f, c, std::make_integer_sequence<int, ge - 1>{});
+    } else {
+      r.acc[K][J][V] = fold_range<S, T, gb>(r.acc[K][J][V], f, c, std::make_integer_sequence<int, ge - gb>{});
+    }
   }
 }
 
 template <typename T, class C, int DM, bool START, int K, int J, int... Vs>
-__device__ __forceinline__ void stream_row(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+__device__ __forceinline__ void stream_row(MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                            std::integer_sequence<int, Vs...>) {
-  (stream_point<T, C, DM, START, K, J, Vs>(r, c), ...);
+  if constexpr (C::PAIR)
+    ((Vs % 2 == 0 ? stream_point<T, C, DM, START, K, J, Vs>(r, c) : void()), ...);
+  else
+    (stream_point<T, C, DM, START, K, J, Vs>(r, c), ...);
 }
 
 template <typename T, class C, int DM, bool START, int K, int... Js>
-__device__ __forceinline__ void stream_slot(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+__device__ __forceinline__ void stream_slot(MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                             std::integer_sequence<int, Js...>) {
   (stream_row<T, C, DM, START, K, Js>(r, c, std::make_integer_sequence<int, C::VX>{}), ...);
 }
 
 // Steady step: the lead plane is offset RM - K of output slot K (slot 2RM starts, slot 0 ends).
 template <typename T, class C, int... Ks>
-__device__ __forceinline__ void stream_apply(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+__device__ __forceinline__ void stream_apply(MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                              std::integer_sequence<int, Ks...>) {
   (stream_slot<T, C, C::RM - Ks, Ks == 2 * C::RM, Ks>(r, c, std::make_integer_sequence<int, C::PY>{}), ...);
 }
@@ -525,14 +544,14 @@ __device__ __forceinline__ void stream_rows(MarchRegs<T, C>& r, const T* const* 
 
 // Warm-up plane PL (< 2RM) of an item: it is offset PL - RM - K of output slot K <= PL.
 template <typename T, class C, int PL, int... Ks>
-__device__ __forceinline__ void stream_warm(MarchRegs<T, C>& r, const Coefs<T, C::shape::NTERMS>& c,
+__device__ __forceinline__ void stream_warm(MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                             std::integer_sequence<int, Ks...>) {
   (stream_slot<T, C, PL - C::RM - Ks, Ks == PL, Ks>(r, c, std::make_integer_sequence<int, C::PY>{}), ...);
 }
 
 template <typename T, class C, int... PLs>
 __device__ __forceinline__ void stream_fill(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
-                                            const Coefs<T, C::shape::NTERMS>& c, std::integer_sequence<int, PLs...>) {
+                                            const EvalCoefs<T, C>& c, std::integer_sequence<int, PLs...>) {
   ((stream_rows<T, C, PLs>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{}),
     stream_warm<T, C, PLs>(r, c, std::make_integer_sequence<int, PLs + 1>{})),
    ...);
@@ -740,7 +759,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
       }
       if constexpr (C::STREAM) {
         if (grp == 0)  // planes mb-RM .. mb+RM-1 start outputs mb .. mb+2RM-1
-          stream_fill<T, C>(r, sb, toff, lane_x, coef, std::make_integer_sequence<int, 2 * C::RM>{});
+          stream_fill<T, C>(r, sb, toff, lane_x, ecoef, std::make_integer_sequence<int, 2 * C::RM>{});
       }
       const long long m_grp = (long long)grp * C::RB;
       const int planes = int(me - mb - m_grp);
