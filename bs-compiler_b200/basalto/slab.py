@@ -22,11 +22,11 @@ k x radius and the slab exchanges once per k sweeps instead of once per sweep; t
 defaults to what the library reports for the program (bst_slab_ghost_depth), capped by the
 smallest rank's owned planes.
 
-Peer transport (transport="peer", bst_slab_sweeps_p2p): no exchange step at all.  The two
-boundary launches of every sweep store their output planes both locally and, through CUDA IPC
-peer mappings over NVLink, straight into the neighbours' ghost planes, then raise a sequence
-flag in the neighbour's memory; the next sweep's boundary launches wait (bounded) for the
-neighbours' flags.  The interior launch runs meanwhile and never reads ghost planes.
+Peer transport (transport="peer", bst_slab_sweeps_p2p): no exchange step at all.  Every
+sweep is one kernel launch whose boundary work items store their output planes both locally
+and, through CUDA IPC peer mappings over NVLink, straight into the neighbours' ghost planes,
+then raise a sequence flag in the neighbour's memory; items that read ghost planes wait
+(bounded) for the neighbours' previous sweep.
 """
 from __future__ import annotations
 

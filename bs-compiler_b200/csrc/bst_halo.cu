@@ -153,27 +153,6 @@ static int wait_comm(bst_comm* c, const char* what) {
     else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
-// Bounded wait (about 2 s) by one thread until the neighbours' flags reach v_lo / v_hi (a null
-// flag is not waited for); on expiry the error word gets kErrPeerTimeout and the wait ends.
-// Queued ahead of the boundary launches, which read the ghost planes the neighbours store here
-// and store into theirs.
-__global__ void wait_peer_kernel(const unsigned long long* f_lo, unsigned long long v_lo,
-                                 const unsigned long long* f_hi, unsigned long long v_hi, unsigned* err) {
-  if (threadIdx.x != 0) return;
-  const uint64_t t0 = global_ns();
-  for (;;) {
-    unsigned long long a = ~0ull, b = ~0ull;
-    if (f_lo) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(f_lo) : "memory");
-    if (f_hi) asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(b) : "l"(f_hi) : "memory");
-    if (a >= v_lo && b >= v_hi) return;
-    if (global_ns() - t0 > 2000000000ull) {
-      atomicOr(err, kErrPeerTimeout);
-      return;
-    }
-    __nanosleep(256);
-  }
-}
-
 // Poll a stream until its work is done, bounded by the communicator's timeout (a neighbour that
 // never joins the NCCL group must not hang the caller).
 static int wait_stream_bounded(bst_comm* c, cudaStream_t st, const char* what) {
@@ -737,64 +716,48 @@ int bst_slab_sweeps_p2p(bst_comm* c, const bst_program* prog, int32_t dtype, int
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   BST_CUDA(cudaSetDevice(c->device));
-  unsigned* err = device_error_word();
-  if (!err) return fail(BST_ERR_CUDA, "device error word unavailable");
   const size_t ghost_bytes = size_t(G) * plane * es;
+  const bool lo = c->nranks > 1 && c->rank > 0, hi = c->nranks > 1 && c->rank < c->nranks - 1;
   int cur = 0;  // index of src in bufs
-  BST_CUDA(cudaEventRecord(c->ev_int, st));
   for (int k = 0; k < nsteps; ++k) {
     char* src = static_cast<char*>(bufs[cur]);
     char* dst = static_cast<char*>(bufs[1 - cur]);
     const bst_comm::PeerSlab* dreg = reg[1 - cur];
     void* out = dst + ghost_bytes;
-    const unsigned long long seq = ++c->seq;
-    BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
-    const bool lo = c->nranks > 1 && c->rank > 0, hi = c->nranks > 1 && c->rank < c->nranks - 1;
-    if (lo || hi) {
-      // The neighbours' previous pass has stored this pass's input ghosts here and is done
-      // reading the ghost planes this pass stores into.
-      wait_peer_kernel<<<1, 32, 0, c->bnd_stream>>>(lo ? c->flags + 0 : nullptr, seq - 1,
-                                                     hi ? c->flags + 1 : nullptr, seq - 1, err);
-      BST_CUDA(cudaGetLastError());
+    // One launch per sweep.  Items holding the first / last G owned planes also store them
+    // into the neighbours' ghost planes and raise their flags when all such items are done;
+    // items reading ghost planes first wait for the neighbours' previous sweep.
+    PeerStore pe{};
+    pe.seq = ++c->seq;
+    pe.wait_value = pe.seq - 1;
+    pe.done = c->flags + 2;
+    pe.lo_end = 0;
+    pe.hi_begin = int(nl);
+    if (lo) {  // owned plane m (< G) -> rank-1's upper ghost plane g_lo + n_lo + m
+      pe.delta_lo = (long long)(intptr_t(dreg->lo) - intptr_t(dst)) +
+                    (long long)(dreg->g_lo + dreg->n_lo - G) * (long long)(plane * es);
+      pe.lo_end = int(G);
+      pe.wait_lo = c->flags + 0;
+      pe.flag_lo = c->flag_lo_remote;
     }
-    BST_CUDA(prof_mark(c, 0, c->bnd_stream));
-    PeerStore p_lo{}, p_hi{};
-    if (lo) {
-      // owned plane m (< G) -> rank-1's upper ghost plane g_lo + n_lo + m
-      p_lo.delta_bytes = (long long)(intptr_t(dreg->lo) - intptr_t(dst)) +
-                         (long long)(dreg->g_lo + dreg->n_lo - G) * (long long)(plane * es);
-      p_lo.done_count = c->flags + 2;
-      p_lo.flag = c->flag_lo_remote;
-      p_lo.seq = seq;
+    if (hi) {  // owned plane m (>= nl - G) -> rank+1's lower ghost plane m - (nl - G)
+      pe.delta_hi = (long long)(intptr_t(dreg->hi) - intptr_t(dst)) - (long long)nl * (long long)(plane * es);
+      pe.hi_begin = int(nl - G);
+      pe.wait_hi = c->flags + 1;
+      pe.flag_hi = c->flag_hi_remote;
     }
-    if (hi) {
-      // owned plane m (>= nl - G) -> rank+1's lower ghost plane m - (nl - G)
-      p_hi.delta_bytes = (long long)(intptr_t(dreg->hi) - intptr_t(dst)) - (long long)nl * (long long)(plane * es);
-      p_hi.done_count = c->flags + 3;
-      p_hi.flag = c->flag_hi_remote;
-      p_hi.seq = seq;
-    }
-    rc = launch_sweep(k_canon, dtype, src, s, out, s, 0, G, c->bnd_stream, lo ? &p_lo : nullptr);
-    if (!rc) rc = launch_sweep(k_canon, dtype, src, s, out, s, nl - G, nl, c->bnd_stream, hi ? &p_hi : nullptr);
+    const bool prof = c->prof_used < c->prof_cap;
+    if (prof)  // the whole sweep is one launch: boundary and exchange ride inside it
+      for (int i = 0; i < 6; ++i)
+        if (i != 5) BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + i], st));
+    rc = launch_sweep(k_canon, dtype, src, s, out, s, 0, nl, st, (lo || hi) ? &pe : nullptr);
     if (rc) return rc;
-    BST_CUDA(prof_mark(c, 1, c->bnd_stream));
-    BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
-    if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
-    BST_CUDA(prof_mark(c, 4, st));
-    if (G < nl - G) {
-      rc = launch_sweep(k_canon, dtype, src, s, out, s, G, nl - G, st);
-      if (rc) return rc;
-    }
-    BST_CUDA(prof_mark(c, 5, st));
-    if (c->prof_used < c->prof_cap) {  // the exchange rides inside the boundary launches
-      BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 2], c->bnd_stream));
-      BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 3], c->bnd_stream));
+    if (prof) {
+      BST_CUDA(cudaEventRecord(c->prof[size_t(c->prof_used) * 6 + 5], st));
       ++c->prof_used;
     }
-    BST_CUDA(cudaEventRecord(c->ev_int, st));
     cur = 1 - cur;
   }
-  if (nsteps > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(nsteps - 1) % 2], 0));
   return BST_OK;
 }
 

@@ -193,7 +193,8 @@ constexpr auto pick_segs() {
 // ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
 // wide radii, dearer in shared-memory bandwidth.
 template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false,
-          bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1, bool PAIR_ = false>
+          bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1, bool PAIR_ = false, bool CIRC_ = false,
+          int INTERLEAVE_ = 0>
 struct MarchCfg {
   using shape = S;
   static constexpr int MINB = MINB_;  // CTAs per SM the register allocation must allow
@@ -222,8 +223,20 @@ struct MarchCfg {
   // Window slots: a group of RB plane steps reads planes g0-WM .. g0+RB-1+WM (g0 = the group's
   // first output plane), so the window holds 2WM+RB planes and shifts by RB once per group.
   static constexpr int WSLOTS = WINDOW ? 2 * WM + RB : 1;
+  // Circular window: instead of shifting the window by RB registers per group, group g uses
+  // the slots of phase g mod PHASES, so a plane stays in one register for its whole life and
+  // the group body exists once per phase (PHASES copies of the code, no register moves).
+  static constexpr bool CIRC = CIRC_ && WINDOW && WSLOTS % RB == 0;
+  static constexpr int PHASES = CIRC ? WSLOTS / RB : 1;
+  // Window register slot of relative slot `rel` (0 = the group's oldest plane) in phase ph.
+  static constexpr int wslot(int ph, int rel) { return CIRC ? (ph * RB + rel) % WSLOTS : rel; }
   // fp32 points evaluated two at a time with paired instructions.
   static constexpr bool PAIR = PAIR_ && sizeof(T) == 4;
+  // Paired folds: 1 = the thread's point pairs of a plane advance term by term together;
+  // 2 = the pairs of all RB planes of a group do (each plane step gets its own row segments).
+  static constexpr int INTERLEAVE = (PAIR && !STREAM) ? INTERLEAVE_ : 0;
+  static constexpr int SEGBANKS = INTERLEAVE == 2 ? RB : 1;
+  static constexpr int bank(int p) { return SEGBANKS > 1 ? p : 0; }
   // Stages read by group g (input planes g*RB + [0, RB-1+2RM] relative to the item's first
   // loaded plane): the window keeps planes behind the current one in registers, so in window
   // mode group g only reads from plane g*RB + RM on and earlier stages retire early.
@@ -270,7 +283,8 @@ struct MarchArgs {
   int balanced;
   unsigned* err;
   int vec_store;  // output rows are 16-byte aligned and contiguous in x
-  PeerStore peer;  // optional second destination on a neighbouring GPU (slab boundary planes)
+  PeerStore peer;  // slab sweeps with peer stores (the PEER kernel); chunks then run last to first, so
+                  // the boundary chunks sit at both ends of the launch
 };
 
 // Balanced contiguous range of CTA b among G CTAs over W units.
@@ -297,26 +311,26 @@ struct Vec16<double> {
 template <typename T, class C>
 struct MarchRegs {
   T win[C::WSLOTS][C::PY][C::VX];
-  T seg[C::NSEG > 0 ? C::NSEG : 1][C::SEGW];
+  T seg[C::SEGBANKS][C::NSEG > 0 ? C::NSEG : 1][C::SEGW];
   T acc[C::STREAM ? 2 * C::RM + 1 : 1][C::PY][C::VX];  // stream mode: outputs g .. g+2RM in flight
 };
 
-// Tap values of point (row J, element V) at plane step P of a group.
-template <typename T, class C, int J, int V, int P = 0>
+// Tap values of point (row J, element V) at plane step P of a group of window phase PH.
+template <typename T, class C, int J, int V, int P = 0, int PH = 0>
 struct PointFetch {
   const MarchRegs<T, C>& r;
   template <int dm, int dy, int dx>
   __device__ __forceinline__ T get() const {
     if constexpr (C::WINDOW && (dm != 0 || (dy == 0 && dx == 0))) {
-      return r.win[P + C::WM + dm][J][V];
+      return r.win[C::wslot(PH, P + C::WM + dm)][J][V];
     } else if constexpr (C::STREAM) {  // every offset reads the current lead plane's rows
       constexpr int k = C::seg_index(C::RM, J + dy);
       static_assert(k >= 0, "tap without a row segment");
-      return r.seg[k][C::HX + V + dx];
+      return r.seg[C::bank(P)][k][C::HX + V + dx];
     } else {
       constexpr int k = C::seg_index(dm, J + dy);
       static_assert(k >= 0, "tap without a row segment");
-      return r.seg[k][C::HX + V + dx];
+      return r.seg[C::bank(P)][k][C::HX + V + dx];
     }
   }
 };
@@ -333,19 +347,19 @@ __device__ __forceinline__ void lds_vec(const T* p, T (&v)[N]) {
 // Load row segment K for the plane whose tile starts at `pl` (dm already applied), at plane
 // step P of a group.  `pl` points at the thread's first vector (row 0 of its rows) in the
 // plane tile.
-template <typename T, class C, int K, int P = 0>
+template <typename T, class C, int K, int P = 0, int PH = 0>
 __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, int /*unused*/, int lane_x) {
   constexpr SegRow R = C::SEGS.r[K];
   const T* rowp = pl + R.srow * C::TXL;
   T own[C::VX];
   if constexpr (C::WINDOW && R.dm == 0 && R.srow >= 0 && R.srow < C::PY) {
 #pragma unroll
-    for (int e = 0; e < C::VX; ++e) own[e] = r.win[P + C::WM][R.srow][e];
+    for (int e = 0; e < C::VX; ++e) own[e] = r.win[C::wslot(PH, P + C::WM)][R.srow][e];
   } else {
     lds_vec<T, C::VX>(rowp, own);
   }
 #pragma unroll
-  for (int e = 0; e < C::VX; ++e) r.seg[K][C::HX + e] = own[e];
+  for (int e = 0; e < C::VX; ++e) r.seg[C::bank(P)][K][C::HX + e] = own[e];
   if constexpr (C::HALO_LDS) {
     // x-halo as whole neighbouring 16-byte vectors straight from the tile (it holds HX
     // loaded columns on each side): one ld.shared.v4 per vector instead of a shuffle and a
@@ -358,7 +372,7 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
       lds_vec<T, C::VX>(rowp + vv * C::VX, nb);
 #pragma unroll
       for (int e = 0; e < C::VX; ++e)
-        if (vv * C::VX + e >= R.lo && vv * C::VX + e <= R.hi) r.seg[K][C::HX + vv * C::VX + e] = nb[e];
+        if (vv * C::VX + e >= R.lo && vv * C::VX + e <= R.hi) r.seg[C::bank(P)][K][C::HX + vv * C::VX + e] = nb[e];
     }
   } else {
     // x-halo from neighbouring lanes; the tile's edge lanes read shared memory.
@@ -367,26 +381,26 @@ __device__ __forceinline__ void load_segment(MarchRegs<T, C>& r, const T* pl, in
       const int d = (-e + C::VX - 1) / C::VX;  // lanes to the left holding element e
       T v = __shfl_up_sync(0xffffffffu, own[e + d * C::VX], d, C::LPR);
       if (lane_x < d) v = rowp[e];
-      r.seg[K][C::HX + e] = v;
+      r.seg[C::bank(P)][K][C::HX + e] = v;
     }
 #pragma unroll
     for (int e = C::VX; e <= R.hi; ++e) {
       const int d = e / C::VX;  // lanes to the right holding element e
       T v = __shfl_down_sync(0xffffffffu, own[e - d * C::VX], d, C::LPR);
       if (lane_x >= C::LPR - d) v = rowp[e];
-      r.seg[K][C::HX + e] = v;
+      r.seg[C::bank(P)][K][C::HX + e] = v;
     }
   }
 }
 
 // Tap values of the points (row J, elements V and V+1) as one pair (PAIR configurations).
-template <class C, int J, int V, int P>
+template <class C, int J, int V, int P, int PH = 0>
 struct PairFetch {
   const MarchRegs<float, C>& r;
   template <int dm, int dy, int dx>
   __device__ __forceinline__ float2 get() const {
-    return make_float2(PointFetch<float, C, J, V, P>{r}.template get<dm, dy, dx>(),
-                       PointFetch<float, C, J, V + 1, P>{r}.template get<dm, dy, dx>());
+    return make_float2(PointFetch<float, C, J, V, P, PH>{r}.template get<dm, dy, dx>(),
+                       PointFetch<float, C, J, V + 1, P, PH>{r}.template get<dm, dy, dx>());
   }
 };
 
@@ -408,7 +422,7 @@ __device__ __forceinline__ EvalCoefs<T, C> eval_coefs(const Coefs<T, C::shape::N
   }
 }
 
-template <typename T, class C, int P, int J, int... Vs>
+template <typename T, class C, int P, int PH, int J, int... Vs>
 __device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const EvalCoefs<T, C>& c, T (&res)[C::VX],
                                          std::integer_sequence<int, Vs...>) {
   if constexpr (C::PAIR) {
@@ -416,14 +430,14 @@ __device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const EvalCoe
     (
         [&] {
           if constexpr (Vs % 2 == 0) {
-            const float2 v = eval_shape<typename C::shape, float2>(PairFetch<C, J, Vs, P>{r}, c);
+            const float2 v = eval_shape<typename C::shape, float2>(PairFetch<C, J, Vs, P, PH>{r}, c);
             res[Vs] = v.x;
             res[Vs + 1] = v.y;
           }
         }(),
         ...);
   } else {
-    ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs, P>{r}, c)), ...);
+    ((res[Vs] = eval_shape<typename C::shape, T>(PointFetch<T, C, J, Vs, P, PH>{r}, c)), ...);
   }
 }
 
@@ -451,20 +465,61 @@ __device__ __forceinline__ void store_row(T* d, const T (&res)[C::VX], bool inte
   }
 }
 
+// Interleaved paired evaluation (INTERLEAVE configurations): the thread's PY x VX/2 point
+// pairs advance term by term together, so consecutive instructions belong to independent
+// fold chains (each chain keeps its own exact order).
+template <typename T, class C, int P, int PH, int G, int J, int... Qs>
+__device__ __forceinline__ void fold_pairs_row(float2 (&a)[C::VX / 2], const MarchRegs<T, C>& r,
+                                               const EvalCoefs<T, C>& c, std::integer_sequence<int, Qs...>) {
+  using S = typename C::shape;
+  if constexpr (G == 0) {
+    ((a[Qs] = eval_term<S, 0, float2>(PairFetch<C, J, 2 * Qs, P, PH>{r}, c)), ...);
+    if (c.init_zero) ((a[Qs] = add_rn(zero_of<float2>(), a[Qs])), ...);
+  } else {
+    ((a[Qs] = fold_term<S, G, float2>(a[Qs], PairFetch<C, J, 2 * Qs, P, PH>{r}, c)), ...);
+  }
+}
+template <typename T, class C, int P, int PH, int G, int... Js>
+__device__ __forceinline__ void fold_pairs_term(float2 (&a)[C::PY][C::VX / 2], const MarchRegs<T, C>& r,
+                                                const EvalCoefs<T, C>& c, std::integer_sequence<int, Js...>) {
+  (fold_pairs_row<T, C, P, PH, G, Js>(a[Js], r, c, std::make_integer_sequence<int, C::VX / 2>{}), ...);
+}
+template <typename T, class C, int P, int PH, int... Gs>
+__device__ __forceinline__ void fold_pairs(float2 (&a)[C::PY][C::VX / 2], const MarchRegs<T, C>& r,
+                                           const EvalCoefs<T, C>& c, std::integer_sequence<int, Gs...>) {
+  (fold_pairs_term<T, C, P, PH, Gs>(a, r, c, std::make_integer_sequence<int, C::PY>{}), ...);
+}
+
 // Evaluate the PY x VX points of one plane step and store them.  `dst` points at the
 // thread's first output of row 0 of this plane.
-template <typename T, class C, int P, int... Js>
+template <typename T, class C, int P, int PH, int... Js>
 __device__ __forceinline__ void eval_store(const MarchRegs<T, C>& r, const EvalCoefs<T, C>& c,
                                            T* __restrict__ dst, long long so1, bool interior, int rows_left,
                                            int cols_left, long long so2, long long pd,
                                            std::integer_sequence<int, Js...>) {
-  (
-      [&] {
-        T res[C::VX];
-        eval_row<T, C, P, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
-        store_row<T, C>(dst + Js * so1, res, interior, Js < rows_left, cols_left, so2, pd);
-      }(),
-      ...);
+  if constexpr (C::INTERLEAVE == 1) {
+    float2 a[C::PY][C::VX / 2];
+    fold_pairs<T, C, P, PH>(a, r, c, std::make_integer_sequence<int, C::shape::NTERMS>{});
+    (
+        [&] {
+          T res[C::VX];
+#pragma unroll
+          for (int q = 0; q < C::VX / 2; ++q) {
+            res[2 * q] = a[Js][q].x;
+            res[2 * q + 1] = a[Js][q].y;
+          }
+          store_row<T, C>(dst + Js * so1, res, interior, Js < rows_left, cols_left, so2, pd);
+        }(),
+        ...);
+  } else {
+    (
+        [&] {
+          T res[C::VX];
+          eval_row<T, C, P, PH, Js>(r, c, res, std::make_integer_sequence<int, C::VX>{});
+          store_row<T, C>(dst + Js * so1, res, interior, Js < rows_left, cols_left, so2, pd);
+        }(),
+        ...);
+  }
 }
 
 // Shared-memory tile of the input plane at offset REL from the group's first input plane.
@@ -473,10 +528,10 @@ __device__ __forceinline__ const T* stage_plane(const T* const* sb) {
   return sb[REL / C::RB] + (REL % C::RB) * C::PLANE;
 }
 
-template <typename T, class C, int P, int... Ks>
+template <typename T, class C, int P, int PH, int... Ks>
 __device__ __forceinline__ void load_segments_at(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                                  std::integer_sequence<int, Ks...>) {
-  (load_segment<T, C, Ks, P>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
+  (load_segment<T, C, Ks, P, PH>(r, stage_plane<T, C, P + C::RM + C::SEGS.r[Ks].dm>(sb) + toff, 0, lane_x), ...);
 }
 
 // ---- stream mode -------------------------------------------------------------------
@@ -567,7 +622,7 @@ __device__ __forceinline__ void stream_store(const MarchRegs<T, C>& r, T* __rest
 
 // One plane step P (0..RB-1) of a group: window lead, segments, evaluate + store (the window
 // shifts once per group, in group_steps).
-template <typename T, class C, int P>
+template <typename T, class C, int P, int PH>
 __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                            const EvalCoefs<T, C>& coef, T* dst, long long so1,
                                            bool interior, int rows_left, int cols_left, long long so2, long long pd) {
@@ -585,27 +640,78 @@ __device__ __forceinline__ void plane_step(MarchRegs<T, C>& r, const T* const* s
     if constexpr (C::WINDOW) {
       const T* pl = stage_plane<T, C, P + C::RM + C::WM>(sb) + toff;
 #pragma unroll
-      for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[P + 2 * C::WM][j]);
+      for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[C::wslot(PH, P + 2 * C::WM)][j]);
     }
     if constexpr (C::NSEG > 0)
-      load_segments_at<T, C, P>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
-    eval_store<T, C, P>(r, coef, dst, so1, interior, rows_left, cols_left, so2, pd,
-                        std::make_integer_sequence<int, C::PY>{});
+      load_segments_at<T, C, P, PH>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+    eval_store<T, C, P, PH>(r, coef, dst, so1, interior, rows_left, cols_left, so2, pd,
+                            std::make_integer_sequence<int, C::PY>{});
   }
 }
 
-template <typename T, class C, int... Ps>
+// Term G of every point pair of every plane of a group (INTERLEAVE == 2).
+template <typename T, class C, int PH, int G, int... Ps>
+__device__ __forceinline__ void fold_group_term(float2 (&a)[C::RB][C::PY][C::VX / 2], const MarchRegs<T, C>& r,
+                                                const EvalCoefs<T, C>& c) {
+  (fold_pairs_term<T, C, Ps, PH, G>(a[Ps], r, c, std::make_integer_sequence<int, C::PY>{}), ...);
+}
+template <typename T, class C, int PH, int... Ps, int... Gs>
+__device__ __forceinline__ void fold_group(float2 (&a)[C::RB][C::PY][C::VX / 2], const MarchRegs<T, C>& r,
+                                           const EvalCoefs<T, C>& c, std::integer_sequence<int, Gs...>) {
+  (fold_group_term<T, C, PH, Gs, Ps...>(a, r, c), ...);
+}
+
+// Bytes from a local output plane m to its copy on a neighbouring GPU (0: none).
+__device__ __forceinline__ long long peer_delta(const PeerStore& p, int m) {
+  return m < p.lo_end ? p.delta_lo : (m >= p.hi_begin ? p.delta_hi : 0ll);
+}
+
+template <typename T, class C, bool PEER, int PH, int... Ps>
 __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
                                             const EvalCoefs<T, C>& coef, T* dst0, long long so0,
                                             long long so1, bool interior, int rows_left, int cols_left,
-                                            long long so2, long long pd, int planes,
+                                            long long so2, const PeerStore& pe, int m0, int planes,
                                             std::integer_sequence<int, Ps...>) {
-  // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
-  ((Ps < planes ? plane_step<T, C, Ps>(r, sb, toff, lane_x, coef, dst0 + Ps * so0, so1, interior, rows_left,
-                                       cols_left, so2, pd)
-                : void()),
-   ...);
-  if constexpr (C::WINDOW) {  // next group: its planes g0+RB-WM .. are slots RB ..
+  if constexpr (C::INTERLEAVE == 2) {
+    // Every plane of the group at once: leads and row segments first, then all point pairs of
+    // all planes fold term by term, then the stores (planes beyond the chunk end are computed
+    // from shared memory the ring holds anyway, and not stored).
+    (
+        [&] {
+          const T* pl = stage_plane<T, C, Ps + C::RM + C::WM>(sb) + toff;
+#pragma unroll
+          for (int j = 0; j < C::PY; ++j) lds_vec<T, C::VX>(pl + j * C::TXL, r.win[C::wslot(PH, Ps + 2 * C::WM)][j]);
+          if constexpr (C::NSEG > 0)
+            load_segments_at<T, C, Ps, PH>(r, sb, toff, lane_x, std::make_integer_sequence<int, C::NSEG>{});
+        }(),
+        ...);
+    float2 a[C::RB][C::PY][C::VX / 2];
+    fold_group<T, C, PH, Ps...>(a, r, coef, std::make_integer_sequence<int, C::shape::NTERMS>{});
+    (
+        [&] {
+          if (Ps < planes) {
+            const long long pd = PEER ? peer_delta(pe, m0 + Ps) : 0ll;
+#pragma unroll
+            for (int j = 0; j < C::PY; ++j) {
+              T res[C::VX];
+#pragma unroll
+              for (int q = 0; q < C::VX / 2; ++q) {
+                res[2 * q] = a[Ps][j][q].x;
+                res[2 * q + 1] = a[Ps][j][q].y;
+              }
+              store_row<T, C>(dst0 + Ps * so0 + j * so1, res, interior, j < rows_left, cols_left, so2, pd);
+            }
+          }
+        }(),
+        ...);
+  } else {
+    // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
+    ((Ps < planes ? plane_step<T, C, Ps, PH>(r, sb, toff, lane_x, coef, dst0 + Ps * so0, so1, interior, rows_left,
+                                             cols_left, so2, PEER ? peer_delta(pe, m0 + Ps) : 0ll)
+                  : void()),
+     ...);
+  }
+  if constexpr (C::WINDOW && !C::CIRC) {  // next group: its planes g0+RB-WM .. are slots RB ..
 #pragma unroll
     for (int k = 0; k < 2 * C::WM; ++k)
 #pragma unroll
@@ -615,23 +721,61 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
   }
 }
 
-// End of a launch that stored into a neighbour's ghost planes: every thread's stores are made
-// visible system-wide, and the CTA that finishes last sets the neighbour's sequence flag to
-// peer.seq (it reads that flag before its next pass touches those planes).
-__device__ __forceinline__ void peer_signal(const PeerStore& p) {
+// The group body of window phase ph (compile-time dispatch over the PHASES bodies).
+template <typename T, class C, bool PEER, int... PHs>
+__device__ __forceinline__ void run_group(int ph, MarchRegs<T, C>& r, const T* const* sb, int toff, int lane_x,
+                                          const EvalCoefs<T, C>& coef, T* dst0, long long so0, long long so1,
+                                          bool interior, int rows_left, int cols_left, long long so2,
+                                          const PeerStore& pe, int m0, int planes,
+                                          std::integer_sequence<int, PHs...>) {
+  ((ph == PHs ? group_steps<T, C, PEER, PHs>(r, sb, toff, lane_x, coef, dst0, so0, so1, interior, rows_left, cols_left,
+                                       so2, pe, m0, planes, std::make_integer_sequence<int, C::RB>{})
+              : void()),
+   ...);
+}
+
+// An item that stored into a neighbour's ghost planes is done: every thread's stores are made
+// visible system-wide, and the item that completes the side's count sets the neighbour's
+// sequence flag (the neighbour reads it before its next pass touches those planes).  Called by
+// the whole CTA.
+__device__ __forceinline__ void peer_item_done(unsigned long long* done, long long items, unsigned long long* flag,
+                                               unsigned long long seq) {
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned long long done = atomicAdd(p.done_count, 1ull) + 1ull;
-    if (done == gridDim.x) {
-      *p.done_count = 0ull;  // every CTA has counted: reset for the next launch
+    const unsigned long long n = atomicAdd(done, 1ull) + 1ull;
+    if (n == (unsigned long long)items) {
+      atomicExch(done, 0ull);  // every item of this side has counted: reset for the next pass
       __threadfence_system();
-      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.flag), "l"(p.seq) : "memory");
+      asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(flag), "l"(seq) : "memory");
     }
   }
 }
 
-template <typename T, class C>
+// Bounded wait (about 2 s, one thread) until a neighbour's flag in this GPU's memory reaches v;
+// on expiry the error word gets kErrPeerTimeout.  The proxy fence lets the TMA loads that follow
+// see the planes the neighbour stored.
+__device__ __forceinline__ void peer_wait(const unsigned long long* f, unsigned long long v, unsigned* err) {
+  unsigned long long x;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(x) : "l"(f) : "memory");
+  if (x < v) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+      __nanosleep(128);
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(x) : "l"(f) : "memory");
+      if (x >= v) break;
+      if (global_ns() - t0 > 2000000000ull) {
+        atomicOr(err, kErrPeerTimeout);
+        break;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// PEER: the Z-slab sweep whose boundary planes also go to the neighbouring GPUs (a.peer);
+// ordinary launches are compiled without that logic.
+template <typename T, class C, bool PEER = false>
 __global__ void __launch_bounds__(C::THREADS, C::MINB)
     march_tma_kernel(const __grid_constant__ CUtensorMap tmap, T* __restrict__ out,
                      const MarchArgs a, const Coefs<T, C::shape::NTERMS> coef) {
@@ -678,7 +822,8 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
       w = seg_end;
     } else {
       tile = w % tiles;
-      mb = g.m_lo + (w / tiles) * a.chunk;
+      const long long c_idx = PEER ? a.work / tiles - 1 - w / tiles : w / tiles;
+      mb = g.m_lo + c_idx * a.chunk;
       me = mb + a.chunk < g.m_hi ? mb + a.chunk : g.m_hi;
       w += gridDim.x;
     }
@@ -699,7 +844,16 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     const bool interior = a.vec_store && x0 + C::TX <= g.no[2] && y0 + C::TY <= g.no[1];
     T* out_item = out + mb * g.so[0] + (long long)yo * g.so[1] + (long long)xo * g.so[2];
 
+    // Peer-store sweeps: the first stage reaching the upper ghost planes waits for the upper
+    // neighbour (deferred to the end of the item); the lower ones are read from the start.
+    bool hi_ready = !PEER || a.peer.wait_hi == nullptr;
     auto issue = [&](int q) {
+      if constexpr (PEER) {
+        if (!hi_ready && int(mb) - C::RM + (q + 1) * C::RB - 1 >= int(g.no[0])) {
+          peer_wait(a.peer.wait_hi, a.peer.wait_value, a.err);
+          hi_ready = true;
+        }
+      }
       const unsigned slot = (q_base + unsigned(q)) % C::NS;
       mbar_expect_tx(&bars[slot], unsigned(C::PLANE * C::RB * sizeof(T)));
       tma_load_3d(ring + size_t(slot) * C::STAGE, &tmap, &bars[slot], cx, cy, L0 + q * C::RB);
@@ -708,6 +862,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     n_issued = qt < C::NS ? qt : C::NS;
     n_waited = 0;
     if (leader) {
+      if (PEER && a.peer.wait_lo && mb - C::RM < 0) peer_wait(a.peer.wait_lo, a.peer.wait_value, a.err);
       fence_proxy_async_smem();
       for (int q = 0; q < n_issued; ++q) issue(q);
     }
@@ -763,12 +918,16 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
       }
       const long long m_grp = (long long)grp * C::RB;
       const int planes = int(me - mb - m_grp);
-      group_steps<T, C>(r, sb, toff, lane_x, ecoef, out_item + m_grp * g.so[0], g.so[0], g.so[1], interior,
-                        rows_left, cols_left, g.so[2], a.peer.delta_bytes, planes,
-                        std::make_integer_sequence<int, C::RB>{});
+      run_group<T, C, PEER>(grp % C::PHASES, r, sb, toff, lane_x, ecoef, out_item + m_grp * g.so[0], g.so[0], g.so[1],
+                      interior, rows_left, cols_left, g.so[2], a.peer, int(mb + m_grp), planes,
+                      std::make_integer_sequence<int, C::PHASES>{});
     }
     if (failed) break;
     q_base += unsigned(qt);
+    if constexpr (PEER) {
+      if (a.peer.flag_lo && mb < a.peer.lo_end) peer_item_done(a.peer.done + 0, a.peer.items_lo, a.peer.flag_lo, a.peer.seq);
+      if (a.peer.flag_hi && me > a.peer.hi_begin) peer_item_done(a.peer.done + 1, a.peer.items_hi, a.peer.flag_hi, a.peer.seq);
+    }
   }
 
   if (failed) {
@@ -785,7 +944,6 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     }
     __syncthreads();
   }
-  if (a.peer.flag) peer_signal(a.peer);  // (also after a failure, so the neighbour does not wait it out)
 }
 
 // ---------------------------------------------------------------------------------

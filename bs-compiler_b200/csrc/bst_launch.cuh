@@ -277,7 +277,7 @@ int launch_march(const LaunchReq& r) {
                     march_l2_promotion(), CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(cr)) + ")");
 
-  auto kern = march_tma_kernel<T, C>;
+  auto kern = r.peer ? march_tma_kernel<T, C, true> : march_tma_kernel<T, C, false>;
 
   MarchArgs a{};
   a.g = make_grid(r);
@@ -289,7 +289,8 @@ int launch_march(const LaunchReq& r) {
   const long long tiles = (long long)a.tiles_x * a.tiles_y;
   a.nm = nm;
   long long grid = 0;
-  switch (march_schedule()) {
+  // Peer-store sweeps count their boundary items, so they use the item schedule.
+  switch (r.peer ? Schedule::kItems : march_schedule()) {
     case Schedule::kBalanced:
       a.balanced = 1;
       a.work = tiles * nm;
@@ -322,7 +323,21 @@ int launch_march(const LaunchReq& r) {
                     : 0;
   if (r.peer) {
     a.peer = *r.peer;
-    if (a.peer.delta_bytes % 16 != 0) a.vec_store = 0;  // the remote rows must be 16-byte aligned too
+    if (a.peer.delta_lo % 16 != 0 || a.peer.delta_hi % 16 != 0) a.vec_store = 0;  // remote rows aligned too
+    // Chunks run last to first: the upper-boundary chunk (which reads the upper neighbour's
+    // planes only at its end) leads, the lower-boundary chunk (which reads the lower neighbour's
+    // planes first) closes the launch.  Count the items storing to each side.
+    const long long nchunks = a.work / tiles;
+    long long lo = 0, hi = 0;
+    for (long long ci = 0; ci < nchunks; ++ci) {
+      const long long b = r.m_lo + ci * a.chunk, e = b + a.chunk < r.m_hi ? b + a.chunk : r.m_hi;
+      if (b < (long long)a.peer.lo_end) ++lo;
+      if (e > (long long)a.peer.hi_begin) ++hi;
+    }
+    a.peer.items_lo = lo * tiles;
+    a.peer.items_hi = hi * tiles;
+    if (a.peer.flag_lo && a.peer.items_lo == 0) return fail(BST_ERR_INVALID, "no item stores to the lower neighbour");
+    if (a.peer.flag_hi && a.peer.items_hi == 0) return fail(BST_ERR_INVALID, "no item stores to the upper neighbour");
   }
   dim3 block(C::THREADS);
   kern<<<unsigned(grid), block, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,

@@ -34,15 +34,26 @@ struct GridDesc {
   int64_t m_lo, m_hi;  // output M range computed by this launch
 };
 
-// A second destination for a launch's stores on a neighbouring GPU (Z-slab boundary planes
-// written straight into the neighbour's ghost planes).  delta_bytes: address of the remote copy
-// minus the local output address (0 = none).  When the launch ends, the last CTA sets *flag
-// (the neighbour's memory) to seq; done_count is a zeroed local counter for that election.
+// A Z-slab sweep whose boundary planes also go to the neighbouring GPUs (peer stores).
+// Output planes [0, lo_end) are stored a second time delta_lo bytes away (the lower
+// neighbour's upper ghost planes, through its peer mapping) and planes [hi_begin, n) delta_hi
+// bytes away (the upper neighbour's lower ghost planes).  Before an item reads planes below 0
+// (above n) it waits until *wait_lo (*wait_hi) >= wait_value: the neighbour's previous pass
+// has stored them here and has finished reading the ghost planes this pass stores into.  When
+// every item that stores to a side is done, the last one sets that neighbour's flag
+// (*flag_lo / *flag_hi) to seq.  done[0] / done[1] count those items (zeroed; the last one
+// resets its counter); items_lo / items_hi are their numbers, from the launcher's work plan.
 struct PeerStore {
-  long long delta_bytes;
-  unsigned long long* done_count;
-  unsigned long long* flag;
+  long long delta_lo, delta_hi;
+  int lo_end, hi_begin;  // output planes (a slab has < 2^31 planes)
+  const unsigned long long* wait_lo;
+  const unsigned long long* wait_hi;
+  unsigned long long wait_value;
+  unsigned long long* done;
+  unsigned long long* flag_lo;
+  unsigned long long* flag_hi;
   unsigned long long seq;
+  long long items_lo, items_hi;
 };
 
 // Runtime scalars of a program (compile-time structure lives in the shape type);

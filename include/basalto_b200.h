@@ -267,13 +267,15 @@ BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t d
  * communicator lives.  (The reference exchanges through NCCL or host staging before each
  * launch, crates/basalto-communication/src/halo_exchange.rs:93-322.)
  *
- * bst_slab_sweeps_p2p: nsteps sweeps over (a, b) like bst_slab_sweeps, without NCCL in the
- * loop.  Per sweep, the two boundary launches (the first and last `ghost` owned planes) store
- * every output both into this rank's buffer and, through the peer mapping, into the
- * neighbours' ghost planes; the last CTA of each boundary launch then sets the neighbour's
- * sequence flag.  The next sweep's boundary launches start after a one-thread wait (bounded,
- * about 2 s; a timeout sets the error bit bst_device_error_check reports) for both neighbours'
- * flags.  The interior launch on `stream` runs concurrently and reads no ghost planes.
+ * bst_slab_sweeps_p2p: nsteps sweeps over (a, b) like bst_slab_sweeps, without NCCL and
+ * without an exchange step: each sweep is ONE launch on `stream`.  The launch's work items that
+ * hold the first / last `ghost` owned planes store those outputs both into this rank's buffer
+ * and, through the peer mapping over NVLink, into the neighbours' ghost planes; when every such
+ * item of a side is done, the last one raises that neighbour's sequence flag.  Items that read
+ * ghost planes first wait (one thread, bounded at about 2 s; a timeout sets the error bit
+ * bst_device_error_check reports) until the neighbour's flag shows its previous sweep, which
+ * both delivered those planes and finished reading the ghost planes this sweep overwrites.
+ * Items run last chunk first, so the waits fall at the two ends of the launch.
  * Every buffer a sweep writes (b, and a when nsteps >= 2) must be registered with this
  * geometry; a's ghost planes must hold the neighbours' planes of the input (for example after
  * bst_halo_exchange).  Each rank must own at least 2 x ghost planes; ghost >= the axis-0
