@@ -8,6 +8,7 @@
 #pragma once
 #include "bst_launch.cuh"
 #include "bst_tb2d.cuh"
+#include "bst_tb3d.cuh"
 
 namespace bst {
 
@@ -284,6 +285,82 @@ int launch_tb2d(const LaunchReq& r) {
   return BST_OK;
 }
 
+// ---- temporally blocked multi-sweep (3-D seven-point shapes) ----------------------------
+template <typename T, class C>
+bool tb3_eligible(const LaunchReq& r) {
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  if (c.ndim != 3 || c.boundary != BST_BOUNDARY_ZERO) return false;
+  if (c.org[1] != 0 || c.org[2] != 0) return false;
+  if (reinterpret_cast<uintptr_t>(r.x) % 16 != 0 || r.xs[2] != 1 || (r.xs[1] * E) % 16 != 0 ||
+      (r.xs[0] * E) % 16 != 0)
+    return false;
+  for (int i = 0; i < 3; ++i)
+    if (c.n[i] >= (int64_t(1) << 30) || c.no[i] >= (int64_t(1) << 30)) return false;
+  if (c.R[0] > 1 || c.R[1] > 1 || c.R[2] > 1) return false;
+  return true;
+}
+
+template <typename T, class C>
+int launch_tb3d(const LaunchReq& r) {
+  if (int rc = peer_unsupported(r, "the temporally blocked kernel")) return rc;
+  const Canon& c = *r.c;
+  constexpr int E = sizeof(T);
+  const long long nm = r.m_hi - r.m_lo;
+  if (nm <= 0) return BST_OK;
+  CUtensorMap map;
+  const cuuint64_t dims[3] = {cuuint64_t(c.n[2]), cuuint64_t(c.n[1]), cuuint64_t(c.n[0])};
+  const cuuint64_t strides[2] = {cuuint64_t(r.xs[1] * E), cuuint64_t(r.xs[0] * E)};
+  const cuuint32_t box[3] = {cuuint32_t(C::TXL), cuuint32_t(C::TYL), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  CUresult cr = enc(&map, tma_dtype<T>(), 3, const_cast<void*>(r.x), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, march_l2_promotion(),
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(BST_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(cr)) + ")");
+  auto kern = march_tb3d_kernel<T, C>;
+  Tb3Args a{};
+  a.g = make_grid(r);
+  a.tiles_x = int((c.no[2] + C::TXO - 1) / C::TXO);
+  a.tiles_y = int((c.no[1] + C::TYO - 1) / C::TYO);
+  const int occ = occupancy(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
+  if (occ <= 0) return fail(BST_ERR_CUDA, "3-D temporally blocked kernel does not fit on an SM");
+  const long long resident = (long long)occ * sm_count();
+  const long long tiles = (long long)a.tiles_x * a.tiles_y;
+  long long nchunks = 1;
+  choose_chunks(tiles, nm, 1, 2 * C::K * C::R + 8, resident, &a.chunk, &nchunks);
+  a.n_items = tiles * nchunks;
+  a.err = device_error_word();
+  if (!a.err) return fail(BST_ERR_CUDA, "device error word unavailable");
+  a.vec_store = (reinterpret_cast<uintptr_t>(r.y) % 16 == 0 && r.ys[2] == 1 && (r.ys[1] * E) % 16 == 0 &&
+                 (r.ys[0] * E) % 16 == 0)
+                    ? 1
+                    : 0;
+  const int64_t big = int64_t(1) << 30;
+  const int64_t lo = r.row_hi < r.row_lo ? 0 : r.row_lo, hi = r.row_hi < r.row_lo ? c.no[0] : r.row_hi;
+  a.row_lo = int(lo < -big ? -big : lo);
+  a.row_hi = int(hi > big ? big : hi);
+  const long long grid = a.n_items < resident ? a.n_items : resident;
+  kern<<<unsigned(grid), C::THREADS, C::SMEM, r.st>>>(map, static_cast<T*>(r.y), a,
+                                                      make_coefs<T, C::shape::NTERMS>(c));
+  BST_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return BST_OK;
+}
+
+#ifndef BST_TB3_ROWS
+#define BST_TB3_ROWS 32  // tile rows = warps per CTA
+#endif
+#ifndef BST_TB3_NSX
+#define BST_TB3_NSX 2
+#endif
+#ifndef BST_TB3_KMAX
+#define BST_TB3_KMAX 2  // sweeps fused per 3-D launch at most (fp32 seven-point shapes)
+#endif
+template <typename T, class S, int K>
+using CfgTb3 = Tb3Cfg<T, S, K, BST_TB3_ROWS, BST_TB3_NSX>;
+
 #ifndef BST_TB_RB
 #define BST_TB_RB 6  // a multiple of the window (2R+1 = 3): one group body, no phase dispatch
 #endif
@@ -303,6 +380,10 @@ template <typename T>
 int tb_max_sweeps(const LaunchReq& r) {
   if (shape_matches<Jacobi2D>(*r.c) && tb_eligible<T, CfgTb<T, Jacobi2D, 2>>(r))
     return sizeof(T) == 4 ? BST_TB_KMAX_F32 : 3;
+  if constexpr (sizeof(T) == 4) {
+    if (!contract_applies(*r.c) && shape_matches<Heat3D>(*r.c) && tb3_eligible<T, CfgTb3<T, Heat3D, 2>>(r))
+      return BST_TB3_KMAX;
+  }
   return 1;
 }
 
@@ -321,6 +402,20 @@ int dispatch_tb(const LaunchReq& r, int k) {
         break;
       default:
         break;
+    }
+  }
+  if constexpr (sizeof(T) == 4) {
+    if (!contract_applies(*r.c) && shape_matches<Heat3D>(*r.c)) {
+      switch (k) {
+        case 2: return launch_tb3d<T, CfgTb3<T, Heat3D, 2>>(r);
+#if BST_TB3_KMAX >= 3
+        case 3: return launch_tb3d<T, CfgTb3<T, Heat3D, 3>>(r);
+#endif
+#if BST_TB3_KMAX >= 4
+        case 4: return launch_tb3d<T, CfgTb3<T, Heat3D, 4>>(r);
+#endif
+        default: break;
+      }
     }
   }
   return fail(BST_ERR_UNSUPPORTED, "no temporally blocked kernel for this request");

@@ -237,3 +237,26 @@ def test_temporally_blocked_sweeps_match_oracle(dtype, shape):
         assert np.array_equal(res.cpu().numpy(), ref), (shape, dtype, n)
         if n >= 3:  # two sweeps cannot fuse and still leave the result in buffer a
             assert b.launch_count() - n0 < n  # sweeps were fused
+
+
+@pytest.mark.parametrize("shape", [(37, 61, 130), (20, 28, 120), (9, 5, 7), (64, 70, 257), (3, 40, 300)])
+def test_temporally_blocked_3d_heat_matches_oracle(shape):
+    """Multi-sweep 3-D heat runs fuse sweeps per launch (march_tb3d_kernel): every sweep count
+    gives the iterated single-sweep result bit for bit.  The shapes cover partial tiles in x and
+    y, grids smaller than one tile and than the level warm-up along z, and rows/columns that end
+    inside a tile's overlap."""
+    b = _basalto()
+    from basalto import program as P
+    x = torch.rand(shape, dtype=torch.float32, generator=torch.Generator().manual_seed(23))
+    prog = P.heat7_3d()
+    for n in (2, 3, 4, 7):
+        a = x.cuda()
+        bb = torch.empty_like(a)
+        n0 = b.launch_count()
+        res = b.sweeps(prog, a, bb, n)
+        torch.cuda.synchronize()
+        assert (res.data_ptr() == bb.data_ptr()) == (n % 2 == 1)
+        ref = O.sweeps(x.numpy(), O.heat7_3d, n)
+        assert np.array_equal(res.cpu().numpy(), ref), (shape, n)
+        if n >= 3:
+            assert b.launch_count() - n0 < n  # sweeps were fused

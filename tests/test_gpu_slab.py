@@ -200,3 +200,23 @@ def test_single_rank_peer_transport_equals_single_grid():
             dom.close()
         ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
         assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("shape,steps", [((40, 33, 130), 5), ((16, 64, 256), 8)])
+def test_single_rank_deep_slab_3d_heat(shape, steps):
+    """One rank, deep ghosts for the 3-D heat step: fused 3-D sweeps on slabs (row range [0, n)
+    as the global ends) give exactly the single-grid bits."""
+    from basalto import program as P
+    from basalto.slab import SlabDomain
+    prog = P.heat7_3d()
+    x = torch.rand(shape, generator=torch.Generator().manual_seed(3))
+    dom = SlabDomain(prog, shape, device="cuda:0")
+    try:
+        assert dom.layout.ghost >= 2
+        dom.load(x)
+        dom.run(steps)
+        got = dom.owned().cpu().numpy()
+    finally:
+        dom.close()
+    ref = O.sweeps(x.numpy(), lambda u: O.eval_program(u, oracle_terms(prog)), steps)
+    assert np.array_equal(got, ref)
