@@ -72,6 +72,8 @@ SIGNATURES = [
       c_void_p, c_void_p]),
     ("bst_stencil_sweeps", c_int32,
      [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_void_p, c_void_p, c_int32, c_void_p]),
+    ("bst_stencil_sweeps_fused", c_int32,
+     [POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     ("bst_device_caps_query", c_int32, [c_int32, POINTER(CDeviceCaps)]),
     ("bst_cache_key", c_int32,
      [c_char_p, c_char_p, c_int32, POINTER(c_int64), POINTER(c_int64), c_int64, POINTER(CDeviceCaps),

@@ -43,17 +43,20 @@ def apply(prog: StencilProgram, x: torch.Tensor, out: torch.Tensor | None = None
     return out
 
 
-def sweeps(prog: StencilProgram, a: torch.Tensor, b: torch.Tensor, nsteps: int, stream=None) -> torch.Tensor:
-    """`nsteps` sweeps ping-ponging a -> b -> a ...; returns the buffer holding the result."""
+def sweeps(prog: StencilProgram, a: torch.Tensor, b: torch.Tensor, nsteps: int, stream=None,
+           max_fused: int = 0) -> torch.Tensor:
+    """`nsteps` sweeps ping-ponging a -> b -> a ...; returns the buffer holding the result.
+    max_fused > 0 fuses up to that many sweeps per launch wherever a temporally blocked kernel
+    exists (0: the library's choice, which fuses only where that is faster)."""
     if not (a.is_cuda and b.is_cuda):
         raise RuntimeError("basalto.sweeps needs CUDA tensors")
     if a.shape != b.shape or a.dtype != b.dtype or not (a.is_contiguous() and b.is_contiguous()):
         raise ValueError("ping-pong buffers must be contiguous tensors of one shape and dtype")
     cp = prog.to_c(a.shape)
     with torch.cuda.device(a.device):
-        _abi.check(_abi.lib().bst_stencil_sweeps(
+        _abi.check(_abi.lib().bst_stencil_sweeps_fused(
             ctypes.byref(cp), _dtype(a), a.dim(), _abi.i64_array(a.shape), ctypes.c_void_p(a.data_ptr()),
-            ctypes.c_void_p(b.data_ptr()), int(nsteps), _stream_ptr(a.device, stream)))
+            ctypes.c_void_p(b.data_ptr()), int(nsteps), int(max_fused), _stream_ptr(a.device, stream)))
     return b if nsteps % 2 else a
 
 

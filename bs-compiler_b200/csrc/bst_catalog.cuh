@@ -350,10 +350,10 @@ int launch_tb3d(const LaunchReq& r) {
 }
 
 #ifndef BST_TB3_ROWS
-#define BST_TB3_ROWS 32  // tile rows = warps per CTA
+#define BST_TB3_ROWS 16  // tile rows = warps per CTA (16: 538 Gpts/s, 24: 449, 32: 504 on heat-7 512^3, 2 sweeps)
 #endif
 #ifndef BST_TB3_NSX
-#define BST_TB3_NSX 2
+#define BST_TB3_NSX 6  // prefetch depth (planes); measured 489 -> 504 Gpts/s from 2 to 6 (heat-7 512^3)
 #endif
 #ifndef BST_TB3_KMAX
 #define BST_TB3_KMAX 2  // sweeps fused per 3-D launch at most (fp32 seven-point shapes)
@@ -376,12 +376,16 @@ using CfgTb = TbCfg<T, S, K, BST_TB_RB, BST_TB_NSX>;
 #endif
 
 // Largest number of sweeps one temporally blocked launch can fuse for this request (1 = none).
+// capability = false: only where fusing is the faster choice — the 3-D kernel (bit-identical,
+// but measured slower than single sweeps of the 94 %-of-HBM march kernel) runs only when a
+// caller asks for fused sweeps (bst_stencil_sweeps_fused, or slabs with deeper ghosts).
 template <typename T>
-int tb_max_sweeps(const LaunchReq& r) {
+int tb_max_sweeps(const LaunchReq& r, bool capability) {
   if (shape_matches<Jacobi2D>(*r.c) && tb_eligible<T, CfgTb<T, Jacobi2D, 2>>(r))
     return sizeof(T) == 4 ? BST_TB_KMAX_F32 : 3;
   if constexpr (sizeof(T) == 4) {
-    if (!contract_applies(*r.c) && shape_matches<Heat3D>(*r.c) && tb3_eligible<T, CfgTb3<T, Heat3D, 2>>(r))
+    if (capability && !contract_applies(*r.c) && shape_matches<Heat3D>(*r.c) &&
+        tb3_eligible<T, CfgTb3<T, Heat3D, 2>>(r))
       return BST_TB3_KMAX;
   }
   return 1;

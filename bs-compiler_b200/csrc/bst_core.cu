@@ -242,8 +242,8 @@ int dispatch_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, co
                  int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
 int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
                  int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
-int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
-int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
+int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], bool capability);
+int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], bool capability);
 int dispatch_tb_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
                     int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
@@ -266,9 +266,10 @@ Schedule march_schedule() {
   return s;
 }
 
-int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]) {
-  if (dtype == BST_F32) return tb_max_f32(c, x, xs, y, ys);
-  if (dtype == BST_F64) return tb_max_f64(c, x, xs, y, ys);
+int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
+                  bool capability) {
+  if (dtype == BST_F32) return tb_max_f32(c, x, xs, y, ys, capability);
+  if (dtype == BST_F64) return tb_max_f64(c, x, xs, y, ys, capability);
   return 1;
 }
 
@@ -430,7 +431,13 @@ int bst_stencil_apply(const bst_program* prog, int32_t dtype, int32_t ndim, cons
 
 int bst_stencil_sweeps(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* shape, void* a,
                        void* b, int32_t nsteps, void* stream) {
+  return bst_stencil_sweeps_fused(prog, dtype, ndim, shape, a, b, nsteps, 0, stream);
+}
+
+int bst_stencil_sweeps_fused(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* shape, void* a,
+                             void* b, int32_t nsteps, int32_t max_fused, void* stream) {
   clear_error();
+  if (max_fused < 0) return fail(BST_ERR_INVALID, "negative max_fused");
   if (!shape) return fail(BST_ERR_INVALID, "null shape");
   if (!a || !b) return fail(BST_ERR_INVALID, "null device pointer");
   if (a == b) return fail(BST_ERR_INVALID, "ping-pong buffers must differ");
@@ -446,7 +453,8 @@ int bst_stencil_sweeps(const bst_program* prog, int32_t dtype, int32_t ndim, con
   // Fuse up to kmax sweeps per launch (temporal blocking) where a kernel exists; keep the
   // number of launches of the same parity as nsteps so the result lands in the buffer the
   // contract names.
-  const int kmax = tb_max_sweeps(c, dtype, a, s, b, s);
+  int kmax = tb_max_sweeps(c, dtype, a, s, b, s, max_fused > 0);
+  if (max_fused > 0 && kmax > max_fused) kmax = max_fused;
   void* src = a;
   void* dst = b;
   for (int k : fuse_plan(nsteps, kmax)) {

@@ -512,7 +512,7 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   // Sweeps fused per exchange: bounded by the kernel and by the ghost depth (k*R planes).
   int kmax = 1;
   if (R > 0 && ghost >= 2 * R) {
-    const int kt = tb_max_sweeps(k_canon, dtype, a, s, b, s);
+    const int kt = tb_max_sweeps(k_canon, dtype, a, s, b, s, true);  // the caller chose the ghost depth
     kmax = kt < ghost / R ? kt : ghost / R;
   }
   const std::vector<int> plan = fuse_plan(nsteps, kmax);

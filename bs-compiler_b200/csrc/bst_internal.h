@@ -57,7 +57,9 @@ int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], 
 // (1 = no fused kernel).  launch_fused: k sweeps of output planes [m_lo, m_hi) in one launch
 // (k == 1 is launch_sweep); intermediate values of planes outside [row_lo, row_hi) (output
 // coordinates) are forced to zero, as a single sweep reads zeros outside the grid.
-int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3]);
+// capability: the kernel's limit; otherwise the default (fusing only where it is faster).
+int tb_max_sweeps(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
+                  bool capability = false);
 int launch_fused(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
                  int k, int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 // Sweeps per launch for nsteps ping-pong sweeps, at most kmax per launch, with a launch

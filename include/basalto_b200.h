@@ -149,6 +149,16 @@ BST_API int bst_stencil_apply_noalloc(const bst_program* prog, int32_t dtype, in
 BST_API int bst_stencil_sweeps(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* shape,
                        void* a, void* b, int32_t nsteps, void* stream);
 
+/* bst_stencil_sweeps with a caller-chosen limit of sweeps per launch: max_fused = 0 is the
+ * library's choice (bst_stencil_sweeps: fuse only where a fused launch is faster), k > 0 fuses
+ * up to k sweeps wherever a temporally blocked kernel exists — including the 3-D seven-point
+ * heat step, whose kernel is bit-identical to single sweeps but measured slower than them on
+ * B200 (it is offered for callers that are bound by HBM traffic elsewhere, e.g. sharing it).
+ * Same ping-pong contract as bst_stencil_sweeps.  No reference counterpart (the reference runs
+ * one sweep per call). */
+BST_API int bst_stencil_sweeps_fused(const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* shape,
+                                     void* a, void* b, int32_t nsteps, int32_t max_fused, void* stream);
+
 /* ---- device identity (crates/basalto-common/src/hardware.rs:8-16,19-57,70-86) ---- */
 typedef struct bst_device_caps {
   int32_t compute_capability_major;

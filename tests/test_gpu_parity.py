@@ -239,24 +239,27 @@ def test_temporally_blocked_sweeps_match_oracle(dtype, shape):
             assert b.launch_count() - n0 < n  # sweeps were fused
 
 
-@pytest.mark.parametrize("shape", [(37, 61, 130), (20, 28, 120), (9, 5, 7), (64, 70, 257), (3, 40, 300)])
-def test_temporally_blocked_3d_heat_matches_oracle(shape):
-    """Multi-sweep 3-D heat runs fuse sweeps per launch (march_tb3d_kernel): every sweep count
-    gives the iterated single-sweep result bit for bit.  The shapes cover partial tiles in x and
-    y, grids smaller than one tile and than the level warm-up along z, and rows/columns that end
-    inside a tile's overlap."""
+@pytest.mark.parametrize("shape,fuses", [((37, 61, 132), True), ((20, 28, 120), True), ((9, 5, 8), True),
+                                          ((64, 70, 256), True), ((3, 40, 300), True), ((11, 30, 130), False)])
+def test_temporally_blocked_3d_heat_matches_oracle(shape, fuses):
+    """Multi-sweep 3-D heat runs with max_fused = 2 fuse sweeps per launch (march_tb3d_kernel):
+    every sweep count gives the iterated single-sweep result bit for bit.  The shapes cover partial
+    tiles in x and y, grids smaller than one tile and than the level warm-up along z, and rows
+    and columns that end inside a tile's overlap; rows of 130 floats are not 16-byte aligned,
+    so that grid runs single sweeps.  (With pairs of sweeps per launch and the result in the
+    buffer the contract names, 2 and 3 sweeps cannot fuse; 4 and more do.)"""
     b = _basalto()
     from basalto import program as P
     x = torch.rand(shape, dtype=torch.float32, generator=torch.Generator().manual_seed(23))
     prog = P.heat7_3d()
-    for n in (2, 3, 4, 7):
+    for n in (2, 3, 4, 5, 7, 8):
         a = x.cuda()
         bb = torch.empty_like(a)
         n0 = b.launch_count()
-        res = b.sweeps(prog, a, bb, n)
+        res = b.sweeps(prog, a, bb, n, max_fused=2)
         torch.cuda.synchronize()
         assert (res.data_ptr() == bb.data_ptr()) == (n % 2 == 1)
         ref = O.sweeps(x.numpy(), O.heat7_3d, n)
         assert np.array_equal(res.cpu().numpy(), ref), (shape, n)
-        if n >= 3:
-            assert b.launch_count() - n0 < n  # sweeps were fused
+        if n >= 4:
+            assert (b.launch_count() - n0 < n) == fuses

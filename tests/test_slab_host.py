@@ -203,16 +203,16 @@ def test_deep_halo_scheme_equals_single_grid(world, case):
 
 
 def test_slab_ghost_depth_query():
-    """bst_slab_ghost_depth (host-only): fused depth k*R for the 2-D Jacobi kernel (k = 4 fp32, 3 fp64) and the
-    3-D fp32 heat kernel (k = 2), R where nothing fuses (fp64 heat, the radius-4 star); SlabDomain's default
-    caps it by the smallest rank's owned planes."""
+    """bst_slab_ghost_depth (host-only): fused depth k*R for the 2-D Jacobi kernel (k = 4 fp32, 3 fp64), R where
+    nothing fuses by default (the 3-D heat kernel fuses only on request, the radius-4 star never); SlabDomain's
+    default caps it by the smallest rank's owned planes."""
     from basalto import _abi
     from basalto import program as P
     from basalto.slab import slab_ghost_depth
     assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 1, _abi.BST_F32) == 4
     assert slab_ghost_depth(P.jacobi5_2d(), (8192, 8192), 8, _abi.BST_F64) == 3
     assert slab_ghost_depth(P.jacobi5_2d(), (12, 8192), 4, _abi.BST_F32) == 3
-    assert slab_ghost_depth(P.heat7_3d(), (64, 64, 64), 2, _abi.BST_F32) == 2
+    assert slab_ghost_depth(P.heat7_3d(), (64, 64, 64), 2, _abi.BST_F32) == 1  # 3-D fusion: opt-in only
     assert slab_ghost_depth(P.heat7_3d(), (64, 64, 64), 2, _abi.BST_F64) == 1
     assert slab_ghost_depth(P.heat7_3d().contracted(), (64, 64, 64), 2, _abi.BST_F32) == 1
     assert slab_ghost_depth(P.star_3d(P.LAPLACIAN8_COEFFS), (64, 64, 64), 2, _abi.BST_F32) == 4
