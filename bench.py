@@ -625,12 +625,15 @@ def run_basalto(args):
     # ---- energy over at least one second of steps ----------------------------------------
     energy = None
     meter = EnergyMeter(local)
-    if meter.nv is not None:
+    if True:  # every rank runs these steps (they exchange ghosts), whether or not its NVML answers
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
-        mj0, t0, n_e = meter.read(), time.perf_counter(), 0
-        while n_e < args.steps or time.perf_counter() - t0 < 1.0:
+        # The same number of steps on every rank (their sweeps exchange with each other): at least
+        # a second's worth by the timed steps' duration, which is already the max over ranks.
+        n_energy = max(args.steps, int(1000.0 / max(ms_step, 1e-3)) + 1)
+        mj0, n_e = meter.read(), 0
+        while n_e < n_energy:
             step()
             n_e += 1
             if n_e % 4 == 0:
@@ -643,7 +646,7 @@ def run_basalto(args):
             dist.all_reduce(t, op=dist.ReduceOp.SUM)
             joules = float(t[0].item())
             n_e = int(t[1].item()) // ws
-        if joules == joules and joules > 0:
+        if joules == joules and joules > 0 and n_e > 0:
             energy = {"joules_per_step": round(joules / n_e, 4),
                       "gpts_per_joule": round(points_job * sweeps * n_e / joules / 1e9, 3),
                       "steps": n_e, "note": "NVML total-energy counter, summed over GPUs, untimed steps"}

@@ -661,9 +661,40 @@ __device__ __forceinline__ void fold_group(float2 (&a)[C::RB][C::PY][C::VX / 2],
   (fold_group_term<T, C, PH, Gs, Ps...>(a, r, c), ...);
 }
 
-// Bytes from a local output plane m to its copy on a neighbouring GPU (0: none).
-__device__ __forceinline__ long long peer_delta(const PeerStore& p, int m) {
-  return m < p.lo_end ? p.delta_lo : (m >= p.hi_begin ? p.delta_hi : 0ll);
+// A finished item's output planes [m0, m1) of its tile, copied to the same place `delta` bytes
+// away (a neighbouring GPU's ghost planes, through its peer mapping).  Called by the whole CTA
+// after its stores; they are still in L2.  16-byte vectors where the rows allow.
+template <typename T, class C>
+__device__ __forceinline__ void peer_copy(T* out, const GridDesc& g, int x0, int y0, long long m0, long long m1,
+                                          long long delta, bool vec) {
+  __syncthreads();  // every thread's stores of the item are done
+  const int rows = (int)(g.no[1] - y0 < C::TY ? g.no[1] - y0 : C::TY);
+  const int cols = (int)(g.no[2] - x0 < C::TX ? g.no[2] - x0 : C::TX);
+  if (m1 <= m0 || rows <= 0 || cols <= 0) return;
+  if (vec && cols == C::TX) {
+    using VT = typename Vec16<T>::type;
+    constexpr int NV = C::TX / C::VX;
+    const long long total = (m1 - m0) * rows * NV;
+    for (long long i = threadIdx.x; i < total; i += C::THREADS) {
+      const int v = int(i % NV);
+      const long long r = i / NV;
+      const int y = int(r % rows);
+      const long long m = m0 + r / rows;
+      const T* src = out + m * g.so[0] + (long long)(y0 + y) * g.so[1] + (long long)(x0 + v * C::VX) * g.so[2];
+      const VT q = *reinterpret_cast<const VT*>(src);
+      *reinterpret_cast<VT*>(reinterpret_cast<char*>(const_cast<T*>(src)) + delta) = q;
+    }
+  } else {
+    const long long total = (m1 - m0) * rows * cols;
+    for (long long i = threadIdx.x; i < total; i += C::THREADS) {
+      const int x = int(i % cols);
+      const long long r = i / cols;
+      const int y = int(r % rows);
+      const long long m = m0 + r / rows;
+      T* src = out + m * g.so[0] + (long long)(y0 + y) * g.so[1] + (long long)(x0 + x) * g.so[2];
+      *reinterpret_cast<T*>(reinterpret_cast<char*>(src) + delta) = *src;
+    }
+  }
 }
 
 template <typename T, class C, bool PEER, int PH, int... Ps>
@@ -690,7 +721,7 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
     (
         [&] {
           if (Ps < planes) {
-            const long long pd = PEER ? peer_delta(pe, m0 + Ps) : 0ll;
+            const long long pd = 0ll;
 #pragma unroll
             for (int j = 0; j < C::PY; ++j) {
               T res[C::VX];
@@ -707,7 +738,7 @@ __device__ __forceinline__ void group_steps(MarchRegs<T, C>& r, const T* const* 
   } else {
     // Planes beyond the chunk end (last group only) are skipped; the check is warp-uniform.
     ((Ps < planes ? plane_step<T, C, Ps, PH>(r, sb, toff, lane_x, coef, dst0 + Ps * so0, so1, interior, rows_left,
-                                             cols_left, so2, PEER ? peer_delta(pe, m0 + Ps) : 0ll)
+                                             cols_left, so2, 0ll)
                   : void()),
      ...);
   }
@@ -775,12 +806,32 @@ __device__ __forceinline__ void peer_wait(const unsigned long long* f, unsigned 
 
 // PEER: the Z-slab sweep whose boundary planes also go to the neighbouring GPUs (a.peer);
 // ordinary launches are compiled without that logic.
+// End of an item of a peer-store sweep: its boundary planes to the neighbours, then the item is
+// counted.
+template <typename T, class C>
+__device__ __forceinline__ void peer_item_end(const MarchArgs* a, T* out, const int* peer_tile) {
+  __syncthreads();
+  const int imb = peer_tile[0], ime = peer_tile[1], ix0 = peer_tile[2], iy0 = peer_tile[3];
+  const PeerStore& p = a->peer;
+  if (p.flag_lo && imb < p.lo_end) {
+    peer_copy<T, C>(out, a->g, ix0, iy0, imb, ime < p.lo_end ? ime : p.lo_end, p.delta_lo, a->vec_store != 0);
+    peer_item_done(p.done + 0, p.items_lo, p.flag_lo, p.seq);
+  }
+  if (p.flag_hi && ime > p.hi_begin) {
+    peer_copy<T, C>(out, a->g, ix0, iy0, imb > p.hi_begin ? imb : p.hi_begin, ime, p.delta_hi, a->vec_store != 0);
+    peer_item_done(p.done + 1, p.items_hi, p.flag_hi, p.seq);
+  }
+}
+
+// The PEER variant is compiled for one CTA per SM: its end-of-item work needs a few registers
+// more, which a two-CTA bound of 64 would have to spill.
 template <typename T, class C, bool PEER = false>
-__global__ void __launch_bounds__(C::THREADS, C::MINB)
+__global__ void __launch_bounds__(C::THREADS, PEER ? 1 : C::MINB)
     march_tma_kernel(const __grid_constant__ CUtensorMap tmap, T* __restrict__ out,
-                     const MarchArgs a, const Coefs<T, C::shape::NTERMS> coef) {
+                     const __grid_constant__ MarchArgs a, const Coefs<T, C::shape::NTERMS> coef) {
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[C::NS];
+  __shared__ int peer_tile[5];  // PEER: item mb, me, x0, y0, first stage reaching the upper ghosts
   T* ring = reinterpret_cast<T*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
 
   const int t = threadIdx.x;
@@ -844,14 +895,15 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     const bool interior = a.vec_store && x0 + C::TX <= g.no[2] && y0 + C::TY <= g.no[1];
     T* out_item = out + mb * g.so[0] + (long long)yo * g.so[1] + (long long)xo * g.so[2];
 
-    // Peer-store sweeps: the first stage reaching the upper ghost planes waits for the upper
-    // neighbour (deferred to the end of the item); the lower ones are read from the start.
-    bool hi_ready = !PEER || a.peer.wait_hi == nullptr;
+    // Peer-store sweeps: the first stage reaching the upper ghost planes (stage pq_hi on) waits
+    // for the upper neighbour, so that wait falls at the end of the item; the lower ghost planes
+    // are read from the start.  The item's coordinates for its end-of-item work are parked in
+    // shared memory, not kept in registers across the item.
     auto issue = [&](int q) {
       if constexpr (PEER) {
-        if (!hi_ready && int(mb) - C::RM + (q + 1) * C::RB - 1 >= int(g.no[0])) {
+        if (q >= peer_tile[4]) {
           peer_wait(a.peer.wait_hi, a.peer.wait_value, a.err);
-          hi_ready = true;
+          peer_tile[4] = 1 << 30;
         }
       }
       const unsigned slot = (q_base + unsigned(q)) % C::NS;
@@ -862,6 +914,15 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     n_issued = qt < C::NS ? qt : C::NS;
     n_waited = 0;
     if (leader) {
+      if constexpr (PEER) {
+        peer_tile[0] = int(mb);
+        peer_tile[1] = int(me);
+        peer_tile[2] = x0;
+        peer_tile[3] = y0;
+        // stage q reaches the upper ghosts when mb - RM + (q + 1) * RB - 1 >= n
+        peer_tile[4] = a.peer.wait_hi ? int(floor_div_c(int(g.no[0]) - int(mb) + C::RM - C::RB + 1 + C::RB - 1, C::RB))
+                                      : (1 << 30);
+      }
       if (PEER && a.peer.wait_lo && mb - C::RM < 0) peer_wait(a.peer.wait_lo, a.peer.wait_value, a.err);
       fence_proxy_async_smem();
       for (int q = 0; q < n_issued; ++q) issue(q);
@@ -924,10 +985,7 @@ __global__ void __launch_bounds__(C::THREADS, C::MINB)
     }
     if (failed) break;
     q_base += unsigned(qt);
-    if constexpr (PEER) {
-      if (a.peer.flag_lo && mb < a.peer.lo_end) peer_item_done(a.peer.done + 0, a.peer.items_lo, a.peer.flag_lo, a.peer.seq);
-      if (a.peer.flag_hi && me > a.peer.hi_begin) peer_item_done(a.peer.done + 1, a.peer.items_hi, a.peer.flag_hi, a.peer.seq);
-    }
+    if constexpr (PEER) peer_item_end<T, C>(&a, out, peer_tile);
   }
 
   if (failed) {

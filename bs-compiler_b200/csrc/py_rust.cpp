@@ -6,7 +6,9 @@
 //                       device_ptr_z)
 // which releases the GIL and raises RuntimeError on failure.  Keyword-only extras of this
 // build: custom_coeffs (the Rust-level `custom_coeffs`), program (a packed bst_program)
-// and stream (a cudaStream_t as int; 0 = synchronous on the legacy default stream).
+// and stream (a cudaStream_t as int).  Without stream the call is synchronous, as the
+// reference's launch is; with one (0 included: torch's default stream) it is queued on that
+// stream and returns at once.
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
@@ -34,7 +36,7 @@ class PyBasaltoInterceptor {
                            const std::vector<int64_t>& strides, std::optional<std::string> job_id,
                            uint64_t device_ptr_x, uint64_t device_ptr_y, uint64_t device_ptr_z,
                            std::optional<std::vector<double>> custom_coeffs, std::optional<py::bytes> program,
-                           uint64_t stream) {
+                           std::optional<uint64_t> stream) {
     if (shape.empty() || shape.size() > 3)
       throw std::runtime_error("only 1-D, 2-D and 3-D are supported (shape has " + std::to_string(shape.size()) +
                                " dims)");
@@ -46,6 +48,10 @@ class PyBasaltoInterceptor {
         throw std::runtime_error("program must be a packed bst_program of " + std::to_string(sizeof(bst_program)) +
                                  " bytes");
     }
+    // A null stream makes the C ABI synchronous; the legacy default stream given explicitly (handle
+    // 0, as torch reports it) is passed as CUDA's own handle for it, cudaStreamLegacy = 0x1.
+    void* st = nullptr;
+    if (stream) st = reinterpret_cast<void*>(*stream == 0 ? uint64_t(0x1) : *stream);
     const double* cc = custom_coeffs ? custom_coeffs->data() : nullptr;
     const int64_t nc = custom_coeffs ? int64_t(custom_coeffs->size()) : 0;
     int rc;
@@ -54,8 +60,7 @@ class PyBasaltoInterceptor {
       rc = bst_interceptor_compile_and_execute(
           h_, op.c_str(), dtype.c_str(), int32_t(shape.size()), shape.data(), strides.data(),
           job_id ? job_id->c_str() : nullptr, device_ptr_x, device_ptr_y, device_ptr_z, cc, nc,
-          program ? reinterpret_cast<const bst_program*>(prog_bytes.data()) : nullptr,
-          reinterpret_cast<void*>(stream));
+          program ? reinterpret_cast<const bst_program*>(prog_bytes.data()) : nullptr, st);
     }
     check(rc);
   }
@@ -79,7 +84,7 @@ PYBIND11_MODULE(_rust, m) {
       .def("compile_and_execute", &PyBasaltoInterceptor::compile_and_execute, py::arg("op"), py::arg("dtype"),
            py::arg("shape"), py::arg("strides"), py::arg("job_id"), py::arg("device_ptr_x"),
            py::arg("device_ptr_y"), py::arg("device_ptr_z"), py::kw_only(), py::arg("custom_coeffs") = py::none(),
-           py::arg("program") = py::none(), py::arg("stream") = 0)
+           py::arg("program") = py::none(), py::arg("stream") = py::none())
       .def("cache_size", &PyBasaltoInterceptor::cache_size)
       .def("cache_hits", &PyBasaltoInterceptor::cache_hits)
       .def("last_cache_key", &PyBasaltoInterceptor::last_cache_key);

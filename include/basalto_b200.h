@@ -200,7 +200,8 @@ BST_API void bst_interceptor_destroy(bst_interceptor* h);
  * the stream.  dtype accepts "float32"/"f32"/"float64"/"f64".  Returns BST_ERR_INVALID
  * for rank > 3, shape/strides length mismatch or null x/y (interceptor.rs:316-324), and
  * BST_ERR_UNSUPPORTED for "matmul*" ops.  When stream is NULL the call is synchronous,
- * as the reference's launch is (crates/basalto-target-nvidia/src/runtime.rs:187). */
+ * as the reference's launch is (crates/basalto-target-nvidia/src/runtime.rs:187); to queue on
+ * the legacy default stream without waiting, pass CUDA's handle for it, cudaStreamLegacy. */
 BST_API int bst_interceptor_compile_and_execute(bst_interceptor* h, const char* op, const char* dtype,
                                         int32_t ndim, const int64_t* shape, const int64_t* strides,
                                         const char* job_id, uint64_t device_ptr_x,
