@@ -25,8 +25,8 @@ parity     after the timed steps, sampled output points (global ends, every rank
 e2e        the same metric through the public API with host buffers: every step copies the
            seeded grid in from pinned host memory, runs the sweeps (basalto.apply +
            basalto.sweeps, the C ABI's bst_stencil_apply + bst_stencil_sweeps; at N > 1
-           bst_halo_exchange + bst_slab_sweeps_deep per rank) and copies the result back, two
-           steps in flight on separate copy streams.
+           bst_halo_exchange + bst_slab_sweeps_deep per rank) and copies the result back, three
+           buffer sets in flight, uploads and downloads on separate copy streams.
            e2e.torch_compile_per_sweep: torch.compile(fn, backend="basalto") called once per
            sweep (the drop-in plugin path), N = 1.
 roofline   the dominant kernel: algorithmic bytes (2 x element size per point: one read + one
@@ -238,22 +238,27 @@ class EnergyMeter:
             return None
 
 
-def pipelined(n_steps, upload, compute, download, stream):
-    """Time n_steps end-to-end steps with two buffer sets in flight.
+E2E_SETS = 3  # device buffer sets of the end-to-end pipeline
 
-    Step k uses set k % 2: its host->device upload runs on one copy stream, its compute on
-    `stream`, its device->host download on a second copy stream (PCIe is full duplex), so step
-    k+1's upload and step k-1's download overlap step k's compute.  Every step still copies its
-    own input in and its own result out inside the timed region.  upload(s), compute(s) and
-    download(s) enqueue on the current stream.  Returns ms per step (CUDA events on `stream`)."""
+
+def pipelined(n_steps, upload, compute, download, stream, nsets=E2E_SETS):
+    """Time n_steps end-to-end steps with nsets buffer sets in flight.
+
+    Step k uses set k % nsets: its host->device upload runs on one copy stream, its compute on
+    `stream`, its device->host download on a second copy stream (PCIe is full duplex).  With
+    three sets the upload of step k+1 and the download of step k-1 overlap each other and step
+    k's compute, and an upload never waits for the download just before it.  Every step still
+    copies its own input in and its own result out inside the timed region.  upload(s),
+    compute(s) and download(s) enqueue on the current stream.  Returns ms per step (CUDA
+    events on `stream`)."""
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_done = [torch.cuda.Event() for _ in range(2)]
-    ev_free = [None, None]
+    ev_in = [torch.cuda.Event() for _ in range(nsets)]
+    ev_done = [torch.cuda.Event() for _ in range(nsets)]
+    ev_free = [None] * nsets
 
     def run(n):
         for k in range(n):
-            s = k % 2
+            s = k % nsets
             with torch.cuda.stream(h2d):
                 if ev_free[s] is not None:
                     h2d.wait_event(ev_free[s])
@@ -272,7 +277,7 @@ def pipelined(n_steps, upload, compute, download, stream):
             if e is not None:
                 stream.wait_event(e)
 
-    run(2)  # warm-up
+    run(nsets)  # warm-up
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
@@ -483,9 +488,15 @@ def run_basalto(args):
         owners = [partition(gshape[0], ws, r) for r in range(ws)]
         my_start, n_local = owners[rank]
         transport = args.transport
-        if transport == "auto":  # peer stores for single-sweep passes; NCCL deep halos where sweeps fuse
-            transport = "nccl" if slab_ghost_depth(prog, gshape, ws, dt) > R[0] else "peer"
+        if transport == "auto":  # NCCL side-stream exchange: measured ahead of peer stores on every 3-D workload
+            transport = "nccl"
         G = slab_ghost_depth(prog, gshape, ws, dt) if transport == "nccl" else R[0]
+        if args.ghost:
+            smallest = min(o[1] for o in owners)
+            if transport != "nccl" or R[0] == 0 or args.ghost % R[0] or not R[0] <= args.ghost <= smallest:
+                raise SystemExit(f"--ghost {args.ghost}: the NCCL transport takes a multiple of the axis-0 radius "
+                                 f"({R[0]}) up to the smallest slab ({smallest} planes)")
+            G = args.ghost
         local_shape = [n_local] + list(gshape[1:])
         plane = int(np.prod(gshape[1:]))
         x0 = torch.zeros([n_local + 2 * G] + list(gshape[1:]), dtype=w.dtype, device=dev)
@@ -651,26 +662,13 @@ def run_basalto(args):
                       "gpts_per_joule": round(points_job * sweeps * n_e / joules / 1e9, 3),
                       "steps": n_e, "note": "NVML total-energy counter, summed over GPUs, untimed steps"}
 
-    # Dominant kernel: the sweep; per pass over this rank's grid.
-    passes = launches if not sharded else slab_passes * args.steps
-    launch_ms = ms_total / max(1, passes)
-    per_launch_bytes = 2 * es * local_points
-    achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
-    peak, peak_src = _peaks()
-    if w.name.startswith("mean3"):
-        kernel = "line_kernel"
-    elif sweeps * args.steps > passes:
-        kernel = "march_tb2d_kernel"  # several sweeps fused per pass
-    else:
-        kernel = "march_tma_kernel"
-
     # ---- per-pass breakdown and halo bandwidth (N > 1) ---------------------------------------
     pass_times = None
     halo = None
     if sharded:
         torch.cuda.synchronize()
         dist.barrier()
-        _abi.check(lib.bst_comm_profile_begin(comm, 2 * slab_passes))
+        _abi.check(lib.bst_comm_profile_begin(comm, 2 * sweeps))  # at most one pass per sweep
         for _ in range(2):
             step()
         out = (ctypes.c_double * 6)()
@@ -678,6 +676,7 @@ def run_basalto(args):
         v = torch.tensor(list(out), dtype=torch.float64, device=dev)
         dist.all_reduce(v, op=dist.ReduceOp.MAX)
         npass = max(1.0, float(v[4].item()))
+        slab_passes = max(1, int(round(npass / 2)))  # the library's own fusion, measured over two steps
         pass_times = {"boundary_ms": round(float(v[0].item()) / npass, 4),
                       "exchange_ms": round(float(v[1].item()) / npass, 4),
                       "interior_ms": round(float(v[2].item()) / npass, 4),
@@ -712,25 +711,36 @@ def run_basalto(args):
                 "note": "nccl_*: one NCCL exchange of the ghost planes timed alone on the device after a sleep kernel "
                         "hides its host enqueue (median of 10, max over ranks)"}
         if transport == "peer":
-            # the exchange rides inside the two boundary launches: their remote stores per pass
-            sent = nbrs * G * plane * es
-            bms = pass_times["boundary_ms"]
-            halo.update({"peer_bytes_stored_per_pass": sent, "boundary_launches_ms": bms,
-                         "peer_store_gbs": round(sent / (bms * 1e-3) / 1e9, 2) if bms > 0 else None,
-                         "peer_note": "per pass the boundary launches compute the first and last ghost-depth planes "
-                                      "and store them over NVLink into the neighbours' ghost planes; peer_store_gbs = "
-                                      "bytes stored remotely / boundary-launch time (compute included)"})
+            halo.update({"peer_bytes_stored_per_pass": nbrs * G * plane * es,
+                         "peer_note": "one launch per sweep: the items holding the first and last ghost-depth "
+                                      "owned planes copy them over NVLink into the neighbours' ghost planes at "
+                                      "their end; the pass span is the whole cost, no separate exchange"})
+
+    # Dominant kernel: the sweep; per pass over this rank's grid.
+    passes = launches if not sharded else slab_passes * args.steps
+    launch_ms = ms_total / max(1, passes)
+    per_launch_bytes = 2 * es * local_points
+    achieved = per_launch_bytes / (launch_ms * 1e-3) / 1e9
+    peak, peak_src = _peaks()
+    if w.name.startswith("mean3"):
+        kernel = "line_kernel"
+    elif sweeps * args.steps > passes:  # several sweeps fused per pass
+        kernel = "march_tb3d_kernel" if len(gshape) == 3 else "march_tb2d_kernel"
+    else:
+        kernel = "march_tma_kernel"
+
 
     # ---- e2e through the public API with host buffers ---------------------------------------
     e2e = None
     if args.e2e_steps > 0 and not sharded:
         host_in = x0.cpu().pin_memory()
         out_shape = prog.out_shape(x0.shape)
-        outs = [torch.empty(out_shape, dtype=w.dtype).pin_memory() for _ in range(2)]
-        ex = [torch.empty_like(x0) for _ in range(2)]
-        ea = [torch.empty(out_shape, dtype=w.dtype, device=dev) if prog.boundary == "zero" else None for _ in range(2)]
-        eb = [torch.empty(out_shape, dtype=w.dtype, device=dev) for _ in range(2)]
-        res = [None, None]
+        outs = [torch.empty(out_shape, dtype=w.dtype).pin_memory() for _ in range(E2E_SETS)]
+        ex = [torch.empty_like(x0) for _ in range(E2E_SETS)]
+        ea = [torch.empty(out_shape, dtype=w.dtype, device=dev) if prog.boundary == "zero" else None
+              for _ in range(E2E_SETS)]
+        eb = [torch.empty(out_shape, dtype=w.dtype, device=dev) for _ in range(E2E_SETS)]
+        res = [None] * E2E_SETS
 
         def up(s):
             ex[s].copy_(host_in, non_blocking=True)
@@ -750,8 +760,8 @@ def run_basalto(args):
                "h2d_bytes_per_step": w.points * es * max(1, ws), "d2h_bytes_per_step": w.out_points * es * max(1, ws),
                "ms_per_step": round(e_ms, 3),
                "path": "basalto.apply + basalto.sweeps (C ABI bst_stencil_apply + bst_stencil_sweeps), pinned host "
-                       "grid copied in and the result copied out every step; two steps in flight on separate copy "
-                       "streams" + ("; every rank a replica, max over ranks" if ws > 1 else "")}
+                       "grid copied in and the result copied out every step; three buffer sets in flight, uploads and "
+                       "downloads on separate copy streams" + ("; every rank a replica, max over ranks" if ws > 1 else "")}
         del ex, ea, eb
         torch.cuda.empty_cache()
         if ws == 1:
@@ -783,13 +793,14 @@ def run_basalto(args):
         # pinned host memory, exchanges their ghosts, runs the sweeps and copies the owned
         # result back.
         host_in = x0[G:G + n_local].cpu().pin_memory()
-        outs = [torch.empty(local_shape, dtype=w.dtype).pin_memory() for _ in range(2)]
-        sx = [x0, torch.zeros_like(x0)]
-        sa = [a, torch.zeros_like(a)]
-        sb = [b, torch.zeros_like(b)]
-        register(sa[1])
-        register(sb[1])
-        res = [None, None]
+        outs = [torch.empty(local_shape, dtype=w.dtype).pin_memory() for _ in range(E2E_SETS)]
+        sx = [x0] + [torch.zeros_like(x0) for _ in range(E2E_SETS - 1)]
+        sa = [a] + [torch.zeros_like(a) for _ in range(E2E_SETS - 1)]
+        sb = [b] + [torch.zeros_like(b) for _ in range(E2E_SETS - 1)]
+        for k in range(1, E2E_SETS):
+            register(sa[k])
+            register(sb[k])
+        res = [None] * E2E_SETS
 
         def up(s):
             sx[s][G:G + n_local].copy_(host_in, non_blocking=True)
@@ -812,7 +823,7 @@ def run_basalto(args):
                "h2d_bytes_per_step": total_bytes, "d2h_bytes_per_step": total_bytes,
                "ms_per_step": round(e_ms, 3),
                "path": "bst_halo_exchange + bst_slab_sweeps_deep per rank, pinned host slab copied in and out "
-                       "each step (bytes summed over ranks), two steps in flight, max over ranks"}
+                       "each step (bytes summed over ranks), three buffer sets in flight, max over ranks"}
 
     # ---- CPU baseline (rank 0, N = 1 only, bounded sample) ------------------------------------
     cpu = None
@@ -876,11 +887,15 @@ def main():
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=6)
     ap.add_argument("--transport", choices=["auto", "nccl", "peer"], default="auto",
-                    help="N > 1 ghost planes: peer = boundary launches store into the neighbours over NVLink "
-                         "(single-sweep passes); nccl = NCCL exchange (deep halos where sweeps fuse); auto = peer "
-                         "unless sweeps fuse")
+                    help="N > 1 ghost planes: nccl = boundary planes first, NCCL exchange on a side stream while "
+                         "the interior computes (deep halos where sweeps fuse); peer = one launch per sweep whose "
+                         "boundary items store into the neighbours over NVLink; auto = nccl")
+    ap.add_argument("--ghost", type=int, default=0,
+                    help="N > 1, NCCL transport: ghost planes per side (a multiple of the axis-0 radius; default: "
+                         "the library's fused depth).  Deeper ghosts let the slab sweeps fuse where a temporally "
+                         "blocked kernel exists (3-D heat: 2 sweeps per exchange with 2 ghost planes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -5,7 +5,9 @@ current stream.  A program outside the compiled shape catalog runs the runtime-t
 whose table is uploaded once per device and then reused, so a repeated call must neither copy
 nor synchronise: here five calls are made while a ~2 s sleep kernel still occupies the stream,
 and they must all return to the host long before it ends (any host synchronisation would wait
-for it).  The results must still equal eager torch bit for bit.
+for it).  The results must still equal eager torch on the CPU bit for bit (eager CUDA torch
+divides by a Python scalar as a multiplication by its reciprocal, so it is not the reference
+for the division term).
 """
 import time
 
@@ -41,4 +43,4 @@ def test_plugin_calls_return_before_the_gpu_finishes():
     host_s = time.perf_counter() - t0
     torch.cuda.synchronize()
     assert host_s < 0.5, f"plugin calls waited for the GPU ({host_s:.2f} s on the host)"
-    assert np.array_equal(y.cpu().numpy(), _odd_stencil(x).cpu().numpy())
+    assert np.array_equal(y.cpu().numpy(), _odd_stencil(x.cpu()).numpy())
