@@ -1082,75 +1082,90 @@ struct WinFetch {
   }
 };
 
+// Vectors per lane and warp chunk: a warp owns LINE_U * 32 consecutive output vectors and
+// issues all their loads before it computes, so each thread keeps LINE_U 16-byte loads in
+// flight (one was too few to cover HBM latency at full occupancy).
+constexpr int LINE_U = 4;
+
 // ORG: input index = output index + ORG + tap (0 for same-size, R for valid region).
 template <typename T, class S, int ORG>
 __global__ void __launch_bounds__(256)
     line_kernel(const T* __restrict__ x, T* __restrict__ y, const LineArgs a,
                 const Coefs<T, S::NTERMS> coef) {
   constexpr int V = Vec16<T>::N;
+  constexpr int U = LINE_U;
   constexpr int R = S::RX;
   constexpr int LW = (R + V - 1) / V;  // neighbour vectors needed on each side (org in [0, R])
   constexpr int LWR = (2 * R + V - 1) / V;
   constexpr int W = V * (1 + LW + LWR);   // window elements, window[0] = x[i0 - LW*V]
   const int lane = threadIdx.x & 31;
   const long long nvec_out = (a.n_out + V - 1) / V;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  // All lanes of a warp iterate together (shuffles), so loop to a warp-uniform bound.
-  const long long base = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
-  for (long long wv = base; wv < nvec_out; wv += stride) {
-    const long long v_idx = wv + lane;  // this lane's output vector
-    const long long i0 = v_idx * V;     // first output index
-    T win[W];
-    // Own vector of the input: x[i0 .. i0+V) (aligned: x base 16-byte aligned, i0 % V == 0).
-    T own[V];
-    const bool own_full = (i0 + V <= a.n_in);
-    if (own_full) {
-      load_vec<T>(x + i0, own);
-    } else {
+  // Warp chunks of U*32 vectors, warp-strided over the grid; all lanes of a warp iterate
+  // together (shuffles), so the loop bound is warp-uniform.
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long ch = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; ch * U * 32 < nvec_out;
+       ch += nwarps) {
+    // Own vectors of the input: x[i0 .. i0+V) (aligned: x base 16-byte aligned, i0 % V == 0).
+    T own[U][V];
 #pragma unroll
-      for (int j = 0; j < V; ++j) own[j] = (i0 + j < a.n_in) ? x[i0 + j] : T(0);
+    for (int u = 0; u < U; ++u) {
+      const long long i0 = ((ch * U + u) * 32 + lane) * V;
+      if (i0 + V <= a.n_in) {
+        load_vec<T>(x + i0, own[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) own[u][j] = (i0 + j < a.n_in) ? x[i0 + j] : T(0);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < V; ++j) win[LW * V + j] = own[j];
-    // Neighbour vectors at lane offsets -LW..-1 and +1..+LWR.
+    for (int u = 0; u < U; ++u) {
+      const long long v_idx = (ch * U + u) * 32 + lane;  // this lane's output vector
+      const long long i0 = v_idx * V;                    // first output index
+      T win[W];
 #pragma unroll
-    for (int l = -LW; l <= LWR; ++l) {
-      if (l == 0) continue;
-      const int src = lane + l;
-      T nb[V];
+      for (int j = 0; j < V; ++j) win[LW * V + j] = own[u][j];
+      // Neighbour vectors at lane offsets -LW..-1 and +1..+LWR; lanes past the warp's edge
+      // read them from memory (cached: the warp's own neighbouring loads).
 #pragma unroll
-      for (int j = 0; j < V; ++j) nb[j] = __shfl_sync(0xffffffffu, own[j], src & 31);
-      if (src < 0 || src > 31) {
-        const long long b = i0 + (long long)l * V;
-        if (b >= 0 && b + V <= a.n_in) {
-          load_vec<T>(x + b, nb);
+      for (int l = -LW; l <= LWR; ++l) {
+        if (l == 0) continue;
+        const int src = lane + l;
+        T nb[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) nb[j] = __shfl_sync(0xffffffffu, own[u][j], src & 31);
+        if (src < 0 || src > 31) {
+          const long long b = i0 + (long long)l * V;
+          if (b >= 0 && b + V <= a.n_in) {
+            load_vec<T>(x + b, nb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < V; ++j) nb[j] = (b + j >= 0 && b + j < a.n_in) ? x[b + j] : T(0);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < V; ++j) win[(LW + l) * V + j] = nb[j];
+      }
+      if (v_idx < nvec_out) {
+        T res[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          // Window index of input (output index + ORG) for this output; taps add dx.
+          WinFetch<T> f{win + LW * V + j + ORG};
+          res[j] = eval_shape<S, T>(f, coef);
+        }
+        if (i0 + V <= a.n_out) {
+          using VT = typename Vec16<T>::type;
+          VT q;
+          T* e = reinterpret_cast<T*>(&q);
+#pragma unroll
+          for (int j = 0; j < V; ++j) e[j] = res[j];
+          *reinterpret_cast<VT*>(y + i0) = q;
         } else {
 #pragma unroll
-          for (int j = 0; j < V; ++j) nb[j] = (b + j >= 0 && b + j < a.n_in) ? x[b + j] : T(0);
+          for (int j = 0; j < V; ++j)
+            if (i0 + j < a.n_out) y[i0 + j] = res[j];
         }
       }
-#pragma unroll
-      for (int j = 0; j < V; ++j) win[(LW + l) * V + j] = nb[j];
-    }
-    if (v_idx >= nvec_out) continue;
-    T res[V];
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-      // Window index of input (output index + ORG) for this output; taps add dx.
-      WinFetch<T> f{win + LW * V + j + ORG};
-      res[j] = eval_shape<S, T>(f, coef);
-    }
-    if (i0 + V <= a.n_out) {
-      using VT = typename Vec16<T>::type;
-      VT q;
-      T* e = reinterpret_cast<T*>(&q);
-#pragma unroll
-      for (int j = 0; j < V; ++j) e[j] = res[j];
-      *reinterpret_cast<VT*>(y + i0) = q;
-    } else {
-#pragma unroll
-      for (int j = 0; j < V; ++j)
-        if (i0 + j < a.n_out) y[i0 + j] = res[j];
     }
   }
 }

@@ -135,6 +135,8 @@ int launch_direct_table(const LaunchReq& r) {
 }
 
 // ---- 1-D line ---------------------------------------------------------------------
+int occupancy(const void* fn, int threads, int smem);  // resident CTAs per SM (cached)
+
 template <typename T, class S, int ORG>
 int launch_line(const LaunchReq& r) {
   if (int rc = peer_unsupported(r, "the 1-D line kernel")) return rc;
@@ -142,8 +144,11 @@ int launch_line(const LaunchReq& r) {
   LineArgs a{r.c->n[2], r.c->no[2]};
   const long long nvec = (a.n_out + V - 1) / V;
   if (nvec <= 0) return BST_OK;
-  long long blocks = (nvec + 255) / 256;
-  const long long cap = (long long)sm_count() * 8;
+  const long long per_block = 256LL * LINE_U;  // vectors one block covers per chunk round
+  long long blocks = (nvec + per_block - 1) / per_block;
+  // One wave of resident blocks; later chunks go round the grid.
+  const int occ = occupancy(reinterpret_cast<const void*>(line_kernel<T, S, ORG>), 256, 0);
+  const long long cap = (long long)sm_count() * (occ > 0 ? occ : 1);
   if (blocks > cap) blocks = cap;
   line_kernel<T, S, ORG><<<unsigned(blocks), 256, 0, r.st>>>(
       static_cast<const T*>(r.x), static_cast<T*>(r.y), a, make_coefs<T, S::NTERMS>(*r.c));
