@@ -240,6 +240,12 @@ class EnergyMeter:
 
 E2E_SETS = 3  # device buffer sets of the end-to-end pipeline
 
+TRANSPORT_NOTE = {
+    "nccl": "NCCL ghost exchange on a side stream, overlapped with the interior",
+    "copy": "ghost planes pushed by the copy engines over NVLink, overlapped with the interior",
+    "peer": "boundary planes stored into the neighbours over NVLink by the sweep kernel",
+}
+
 
 def pipelined(n_steps, upload, compute, download, stream, nsets=E2E_SETS):
     """Time n_steps end-to-end steps with nsets buffer sets in flight.
@@ -490,11 +496,11 @@ def run_basalto(args):
         transport = args.transport
         if transport == "auto":  # NCCL side-stream exchange: measured ahead of peer stores on every 3-D workload
             transport = "nccl"
-        G = slab_ghost_depth(prog, gshape, ws, dt) if transport == "nccl" else R[0]
+        G = slab_ghost_depth(prog, gshape, ws, dt) if transport != "peer" else R[0]
         if args.ghost:
             smallest = min(o[1] for o in owners)
-            if transport != "nccl" or R[0] == 0 or args.ghost % R[0] or not R[0] <= args.ghost <= smallest:
-                raise SystemExit(f"--ghost {args.ghost}: the NCCL transport takes a multiple of the axis-0 radius "
+            if transport == "peer" or R[0] == 0 or args.ghost % R[0] or not R[0] <= args.ghost <= smallest:
+                raise SystemExit(f"--ghost {args.ghost}: the NCCL and copy transports take a multiple of the axis-0 radius "
                                  f"({R[0]}) up to the smallest slab ({smallest} planes)")
             G = args.ghost
         local_shape = [n_local] + list(gshape[1:])
@@ -516,10 +522,11 @@ def run_basalto(args):
         comm = h
         cp = prog.to_c(local_shape)
         shp = _abi.i64_array(local_shape)
-        sweep_fn = lib.bst_slab_sweeps_deep if transport == "nccl" else lib.bst_slab_sweeps_p2p
+        sweep_fn = {"nccl": lib.bst_slab_sweeps_deep, "copy": lib.bst_slab_sweeps_copy,
+                    "peer": lib.bst_slab_sweeps_p2p}[transport]
 
         def register(buf):  # collective: every rank registers its buffers in the same order
-            if transport == "peer":
+            if transport != "nccl":
                 _abi.check(lib.bst_comm_register_slab(comm, ctypes.c_void_p(buf.data_ptr()), dt, plane, n_local, G))
 
         register(a)
@@ -539,7 +546,7 @@ def run_basalto(args):
         def step():
             return step_on(x0, a, b)
 
-        kmax = max(1, G // R[0]) if R[0] and transport == "nccl" else 1
+        kmax = max(1, G // R[0]) if R[0] and transport != "peer" else 1
         slab_passes = 1 + len(fuse_plan(sweeps - 1, kmax))
         local_points = n_local * plane
         points_job = int(np.prod(gshape))
@@ -710,6 +717,13 @@ def run_basalto(args):
                 "exchanges_per_step": slab_passes,
                 "note": "nccl_*: one NCCL exchange of the ghost planes timed alone on the device after a sleep kernel "
                         "hides its host enqueue (median of 10, max over ranks)"}
+        if transport == "copy":
+            sent, cms = nbrs * G * plane * es, pass_times["exchange_ms"]
+            halo.update({"copy_bytes_sent_per_pass": sent, "copy_ms": cms,
+                         "copy_nvlink_gbs": round(sent / (cms * 1e-3) / 1e9, 2) if cms > 0 else None,
+                         "copy_note": "per pass: cudaMemcpyAsync of the first and last ghost-depth owned planes "
+                                      "into the neighbours' ghost planes (copy engines, peer mappings) plus the "
+                                      "one-thread flag kernel, timed on the comm stream during the sweeps"})
         if transport == "peer":
             halo.update({"peer_bytes_stored_per_pass": nbrs * G * plane * es,
                          "peer_note": "one launch per sweep: the items holding the first and last ghost-depth "
@@ -847,7 +861,7 @@ def run_basalto(args):
             "config": {"workload": w.label(),
                        "global_grid": "x".join(map(str, gshape)),
                        "parallelism": (f"z-slab x{ws} ({scaling} scaling, {G} ghost planes per side, "
-                                       f"{'boundary planes stored into the neighbours over NVLink' if transport == 'peer' else 'NCCL ghost exchange'})"
+                                       f"{TRANSPORT_NOTE[transport]})"
                                        if sharded
                                        else (f"{ws} independent replicas" if ws > 1 else "single GPU")),
                        "arithmetic": "fused multiply-add fold (BST_PROGRAM_CONTRACT)" if w.program.contract
@@ -888,12 +902,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
     ap.add_argument("--e2e-steps", type=int, default=6)
-    ap.add_argument("--transport", choices=["auto", "nccl", "peer"], default="auto",
+    ap.add_argument("--transport", choices=["auto", "nccl", "copy", "peer"], default="auto",
                     help="N > 1 ghost planes: nccl = boundary planes first, NCCL exchange on a side stream while "
-                         "the interior computes (deep halos where sweeps fuse); peer = one launch per sweep whose "
+                         "the interior computes (deep halos where sweeps fuse); copy = the same passes with the "
+                         "ghost planes pushed by the copy engines over NVLink; peer = one launch per sweep whose "
                          "boundary items store into the neighbours over NVLink; auto = nccl")
     ap.add_argument("--ghost", type=int, default=0,
-                    help="N > 1, NCCL transport: ghost planes per side (a multiple of the axis-0 radius; default: "
+                    help="N > 1, NCCL or copy transport: ghost planes per side (a multiple of the axis-0 radius; default: "
                          "the library's fused depth).  Deeper ghosts let the slab sweeps fuse where a temporally "
                          "blocked kernel exists (3-D heat: 2 sweeps per exchange with 2 ghost planes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

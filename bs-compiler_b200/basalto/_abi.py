@@ -104,6 +104,9 @@ SIGNATURES = [
     ("bst_slab_sweeps_p2p", c_int32,
      [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
       c_void_p]),
+    ("bst_slab_sweeps_copy", c_int32,
+     [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
+      c_void_p]),
     ("bst_comm_profile_begin", c_int32, [c_void_p, c_int32]),
     ("bst_comm_profile_end", c_int32, [c_void_p, POINTER(c_double)]),
 ]

@@ -22,11 +22,20 @@ k x radius and the slab exchanges once per k sweeps instead of once per sweep; t
 defaults to what the library reports for the program (bst_slab_ghost_depth), capped by the
 smallest rank's owned planes.
 
+Copy transport (transport="copy", bst_slab_sweeps_copy): the same passes as the NCCL path,
+with the ghost planes pushed by the copy engines over NVLink (cudaMemcpyAsync into CUDA IPC
+peer mappings of the neighbours' buffers) and a sequence flag raised in the neighbours'
+memory; the boundary rows of the next pass wait (bounded, on the GPU) for those flags.  The
+copies take no SMs, so they overlap an interior launch that holds all of them.
+
 Peer transport (transport="peer", bst_slab_sweeps_p2p): no exchange step at all.  Every
-sweep is one kernel launch whose boundary work items store their output planes both locally
-and, through CUDA IPC peer mappings over NVLink, straight into the neighbours' ghost planes,
-then raise a sequence flag in the neighbour's memory; items that read ghost planes wait
-(bounded) for the neighbours' previous sweep.
+sweep is one kernel launch whose boundary work items copy their output planes, through the
+peer mappings, straight into the neighbours' ghost planes, then raise a sequence flag in the
+neighbour's memory; items that read ghost planes wait (bounded) for the neighbours' previous
+sweep.
+
+With the copy and peer transports the neighbours write into this rank's buffers
+asynchronously: load() belongs before the first run().
 """
 from __future__ import annotations
 
@@ -152,8 +161,9 @@ class SlabDomain:
                  timeout_s: float = 120.0, group=None, ghost: int | None = None, transport: str = "nccl"):
         import torch.distributed as dist
 
-        if transport not in ("nccl", "peer"):
-            raise ValueError("transport is 'nccl' (exchange over NCCL) or 'peer' (boundary stores over NVLink)")
+        if transport not in ("nccl", "copy", "peer"):
+            raise ValueError("transport is 'nccl' (exchange over NCCL), 'copy' (copy engines over NVLink) or "
+                             "'peer' (boundary stores over NVLink)")
         self.transport = transport
         if program.boundary != "zero" or program.ndim not in (2, 3) or program.ndim != len(global_shape):
             raise ValueError("slab sweeps need a same-size 2-D or 3-D program")
@@ -165,7 +175,7 @@ class SlabDomain:
         self._dt = _abi.BST_F32 if dtype == torch.float32 else _abi.BST_F64
         if ghost is None:
             # peer transport sweeps one step per pass: ghosts as deep as the axis-0 radius
-            ghost = slab_ghost_depth(program, gshape, ws, self._dt) if transport == "nccl" else program.radius()[0]
+            ghost = slab_ghost_depth(program, gshape, ws, self._dt) if transport != "peer" else program.radius()[0]
         self.layout = SlabLayout(gshape, ws, rank, int(ghost))
         if self.layout.ghost < program.radius()[0]:
             raise ValueError("ghost depth is below the program's axis-0 radius")
@@ -187,7 +197,7 @@ class SlabDomain:
             _abi.check(_abi.lib().bst_comm_create(uid, ws, rank, self.device.index, float(timeout_s), ctypes.byref(h)))
         self._comm = h
         self.current = self.a
-        if transport == "peer":  # collective: every rank registers its two buffers in this order
+        if transport != "nccl":  # collective: every rank registers its two buffers in this order
             for buf in (self.a, self.b):
                 with torch.cuda.device(self.device):
                     _abi.check(_abi.lib().bst_comm_register_slab(self._comm, ctypes.c_void_p(buf.data_ptr()), self._dt,
@@ -217,7 +227,8 @@ class SlabDomain:
         """nsteps sweeps; returns the buffer holding the result (ghosts valid)."""
         L = self.layout
         other = self.b if self.current is self.a else self.a
-        fn = _abi.lib().bst_slab_sweeps_deep if self.transport == "nccl" else _abi.lib().bst_slab_sweeps_p2p
+        fn = {"nccl": _abi.lib().bst_slab_sweeps_deep, "copy": _abi.lib().bst_slab_sweeps_copy,
+              "peer": _abi.lib().bst_slab_sweeps_p2p}[self.transport]
         with torch.cuda.device(self.device):
             _abi.check(fn(
                 self._comm, ctypes.byref(self._cprog), self._dt, len(L.local_shape), _abi.i64_array(L.local_shape),

@@ -493,9 +493,33 @@ int bst_slab_ghost_depth(const bst_program* prog, int32_t dtype, int32_t ndim, c
   return BST_OK;
 }
 
-int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
-                         const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps, void* stream) {
-  clear_error();
+}  // extern "C"
+
+namespace bst {
+
+// Copy-engine transport kernels.  The wait is one thread polling this GPU's flags for the
+// neighbours' previous pass (bounded, like the peer-store kernel's); the set is one thread
+// storing this pass's sequence number into the neighbours' flags after the copies ahead of it
+// on the same stream have completed.
+__global__ void slab_flags_wait_kernel(const unsigned long long* f_lo, const unsigned long long* f_hi,
+                                       unsigned long long v, unsigned* err) {
+  if (threadIdx.x != 0) return;
+  if (f_lo) peer_wait(f_lo, v, err);
+  if (f_hi) peer_wait(f_hi, v, err);
+}
+
+__global__ void slab_flags_set_kernel(unsigned long long* r_lo, unsigned long long* r_hi, unsigned long long v) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  if (r_lo) asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(r_lo), "l"(v) : "memory");
+  if (r_hi) asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(r_hi), "l"(v) : "memory");
+}
+
+enum class SlabTransport { kNccl, kCopy };
+
+// Overlapped slab passes (boundary rows, ghost transfer, interior rows) for both transports.
+static int slab_passes(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim, const int64_t* local_shape,
+                       int32_t ghost, void* a, void* b, int32_t nsteps, void* stream, SlabTransport tr) {
   if (!c || !prog || !local_shape || !a || !b) return fail(BST_ERR_INVALID, "null argument");
   if (a == b) return fail(BST_ERR_INVALID, "ping-pong slabs must differ");
   if (nsteps < 0) return fail(BST_ERR_INVALID, "negative step count");
@@ -533,6 +557,25 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   char* src = static_cast<char*>(a);
   char* dst = static_cast<char*>(b);
   const size_t ghost_bytes = size_t(ghost) * plane * es;
+  const bool copy = tr == SlabTransport::kCopy && c->nranks > 1 && gx > 0;
+  const bool has_lo = c->rank > 0, has_hi = c->rank < c->nranks - 1;
+  // Copy transport: both buffers are registered slabs (the neighbours' mappings of the same
+  // slot are where this rank's boundary planes go).
+  const bst_comm::PeerSlab* reg[2] = {nullptr, nullptr};
+  if (copy) {
+    void* bufs[2] = {a, b};
+    for (int i = 0; i < 2; ++i) {
+      for (const auto& ps : c->slabs)
+        if (ps.local == bufs[i] && ps.n_local == nl && ps.plane == plane && ps.ghost == ghost && size_t(ps.es) == es)
+          reg[i] = &ps;
+      if (!reg[i] && (i == 1 ? nsteps >= 1 : nsteps >= 2))
+        return fail(BST_ERR_INVALID, "bst_slab_sweeps_copy: every buffer it writes must be registered with "
+                                     "bst_comm_register_slab (same geometry)");
+    }
+    if (!c->flags) return fail(BST_ERR_INVALID, "bst_slab_sweeps_copy: no slab is registered on this communicator");
+  }
+  unsigned* err = copy ? device_error_word() : nullptr;
+  if (copy && !err) return fail(BST_ERR_CUDA, "device error word unavailable");
   const int64_t lo_end = std::min<int64_t>(gx, nl);
   const int64_t hi_begin = std::max<int64_t>(nl - gx, lo_end);
   // Per pass k (src -> dst): the boundary rows run on the high-priority boundary stream,
@@ -541,13 +584,29 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
   //   exchange k  (comm stream) waits for boundary k;
   //   interior k  waits for boundary k-1 (ev_b[(k-1) % 2]; its rows are inside what interior k reads).
   // Events are waited on before they are re-recorded, so every wait sees the intended pass.
+  // Copy transport, per pass k with sequence number q: the boundary stream first waits (bounded,
+  // on the GPU) until both neighbours have raised their flags to q - 1, i.e. their copies of
+  // pass k-1 into src's ghost planes have landed and they are done reading the ghost planes
+  // that this pass's copies overwrite; after the boundary rows, the comm stream copies the
+  // first / last `ghost` owned planes into the neighbours' ghost planes with the copy engines
+  // (no SMs) and raises the neighbours' flags to q; the interior rows wait for the boundary
+  // rows, so the copies overlap the interior launch, which holds every SM.
   const bool exchange = c->nranks > 1 && gx > 0;
   BST_CUDA(cudaEventRecord(c->ev_int, st));  // src (with its ghosts) is ready on the caller's stream
   int k = 0;
+  int cur = 0;  // index of src in {a, b}
   for (int kk : plan) {
     void* out = dst + ghost_bytes;
+    unsigned long long q = 0;
+    if (copy) {
+      q = ++c->seq;
+      if (k > 0) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));  // own copies out of dst
+      slab_flags_wait_kernel<<<1, 32, 0, c->bnd_stream>>>(has_lo ? c->flags + 0 : nullptr,
+                                                          has_hi ? c->flags + 1 : nullptr, q - 1, err);
+      BST_CUDA(cudaGetLastError());
+    }
     BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
-    if (k > 0 && exchange) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
+    if (k > 0 && exchange && !copy) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
     BST_CUDA(prof_mark(c, 0, c->bnd_stream));
     rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
     if (!rc && hi_begin < nl)
@@ -558,12 +617,28 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
     if (exchange) {
       BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
       BST_CUDA(prof_mark(c, 2, c->comm_stream));
-      rc = halo_enqueue(c, dst, dtype, plane, nl, int32_t(gx), c->comm_stream);
-      if (rc) return rc;
+      if (copy) {
+        const bst_comm::PeerSlab* dr = reg[1 - cur];
+        const size_t pb = size_t(plane) * es;
+        // owned planes [0, gx) -> rank-1's upper ghost planes; [nl - gx, nl) -> rank+1's lower ones
+        if (has_lo)
+          BST_CUDA(cudaMemcpyAsync(dr->lo + size_t(dr->g_lo + dr->n_lo) * pb, dst + ghost_bytes, size_t(gx) * pb,
+                                   cudaMemcpyDeviceToDevice, c->comm_stream));
+        if (has_hi)
+          BST_CUDA(cudaMemcpyAsync(dr->hi + size_t(dr->g_hi - gx) * pb, dst + ghost_bytes + size_t(nl - gx) * pb,
+                                   size_t(gx) * pb, cudaMemcpyDeviceToDevice, c->comm_stream));
+        slab_flags_set_kernel<<<1, 32, 0, c->comm_stream>>>(has_lo ? c->flag_lo_remote : nullptr,
+                                                            has_hi ? c->flag_hi_remote : nullptr, q);
+        BST_CUDA(cudaGetLastError());
+      } else {
+        rc = halo_enqueue(c, dst, dtype, plane, nl, int32_t(gx), c->comm_stream);
+        if (rc) return rc;
+      }
       BST_CUDA(prof_mark(c, 3, c->comm_stream));
       BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
     }
-    if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
+    if (copy) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[k % 2], 0));  // boundary rows first (see above)
+    else if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
     BST_CUDA(prof_mark(c, 4, st));
     if (lo_end < hi_begin) {
       rc = launch_fused(k_canon, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
@@ -579,6 +654,7 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
     }
     BST_CUDA(cudaEventRecord(c->ev_int, st));
     std::swap(src, dst);
+    cur = 1 - cur;
     ++k;
   }
   if (k > 0) {
@@ -586,6 +662,22 @@ int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, in
     if (exchange) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
   }
   return BST_OK;
+}
+
+}  // namespace bst
+
+extern "C" {
+
+int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                         const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps, void* stream) {
+  clear_error();
+  return slab_passes(c, prog, dtype, ndim, local_shape, ghost, a, b, nsteps, stream, SlabTransport::kNccl);
+}
+
+int bst_slab_sweeps_copy(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                         const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps, void* stream) {
+  clear_error();
+  return slab_passes(c, prog, dtype, ndim, local_shape, ghost, a, b, nsteps, stream, SlabTransport::kCopy);
 }
 
 int bst_comm_profile_begin(bst_comm* c, int32_t max_passes) {

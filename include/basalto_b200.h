@@ -280,9 +280,9 @@ BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t d
  *
  * bst_slab_sweeps_p2p: nsteps sweeps over (a, b) like bst_slab_sweeps, without NCCL and
  * without an exchange step: each sweep is ONE launch on `stream`.  The launch's work items that
- * hold the first / last `ghost` owned planes store those outputs both into this rank's buffer
- * and, through the peer mapping over NVLink, into the neighbours' ghost planes; when every such
- * item of a side is done, the last one raises that neighbour's sequence flag.  Items that read
+ * hold the first / last `ghost` owned planes, once their outputs are written, copy those planes
+ * of their tile through the peer mapping over NVLink into the neighbours' ghost planes; when
+ * every such item of a side is done, the last one raises that neighbour's sequence flag.  Items that read
  * ghost planes first wait (one thread, bounded at about 2 s; a timeout sets the error bit
  * bst_device_error_check reports) until the neighbour's flag shows its previous sweep, which
  * both delivered those planes and finished reading the ghost planes this sweep overwrites.
@@ -299,8 +299,21 @@ BST_API int bst_slab_sweeps_p2p(bst_comm* c, const bst_program* prog, int32_t dt
                                 const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
                                 void* stream);
 
+/* bst_slab_sweeps_copy: bst_slab_sweeps_deep (same passes, fusion, contract and ghost depth)
+ * with the ghost planes moved by the GPUs' copy engines over NVLink instead of NCCL, on slabs
+ * registered with bst_comm_register_slab (a and b, as for bst_slab_sweeps_p2p).  Per pass:
+ * the boundary rows run first, after a one-thread wait (bounded at about 2 s; a timeout sets
+ * the error bit bst_device_error_check reports) for both neighbours' flags to show their
+ * previous pass; then cudaMemcpyAsync copies the first / last `ghost` owned planes into the
+ * neighbours' ghost planes (through the peer mappings) and a one-thread kernel raises the
+ * neighbours' flags, while the interior rows compute on every SM (the copy engines need none).
+ * All ranks must issue the same sequence of slab calls on the communicator. */
+BST_API int bst_slab_sweeps_copy(bst_comm* c, const bst_program* prog, int32_t dtype, int32_t ndim,
+                                 const int64_t* local_shape, int32_t ghost, void* a, void* b, int32_t nsteps,
+                                 void* stream);
+
 /* Per-pass timing of the slab sweeps (diagnostics).  After bst_comm_profile_begin, the next
- * max_passes passes of bst_slab_sweeps_deep on this communicator record CUDA timing events
+ * max_passes passes of bst_slab_sweeps_deep / _copy / _p2p on this communicator record CUDA timing events
  * around their boundary launches, their ghost exchange and their interior launch.
  * bst_comm_profile_end waits for those events and returns, summed over the recorded passes:
  * out[0] boundary-launch ms, out[1] exchange ms, out[2] interior-launch ms, out[3] pass span ms

@@ -2,8 +2,9 @@
 
 * one rank (an NCCL communicator of size 1): the boundary/interior split and the slab
   addressing must give exactly the single-grid result;
-* two and four ranks on as many GPUs (skipped with fewer): ghost exchange over NCCL,
-  gathered result equal to the single-grid oracle.  NVLS is off; ranks exchange the NCCL id over gloo; every wait
+* two and four ranks on as many GPUs (skipped with fewer): ghost planes over NCCL, over the
+  copy engines, or stored by the sweep kernel itself; gathered result equal to the
+  single-grid oracle.  NVLS is off; ranks exchange the NCCL id over gloo; every wait
   is bounded by process-group and join timeouts.
 """
 import os
@@ -122,7 +123,7 @@ def _rank(rank, world, port, q, transport="nccl"):
     try:
         from basalto.slab import SlabDomain
         res = []
-        for prog, shape, dtype, steps in (_programs() if transport == "nccl" else _peer_programs()):
+        for prog, shape, dtype, steps in (_programs() if transport != "peer" else _peer_programs()):
             x = torch.randn(shape, dtype=dtype, generator=torch.Generator().manual_seed(41))
             dom = SlabDomain(prog, shape, dtype=dtype, device=f"cuda:{rank}", timeout_s=60.0, transport=transport)
             try:
@@ -170,6 +171,19 @@ def test_ranks_nccl_exchange_equals_single_grid(world):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     res, procs = _spawn(world, "nccl")
+    assert res == [True] * len(_programs())
+    assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ranks_copy_engine_transport_equals_single_grid(world):
+    """The NCCL path's passes (deep ghosts and fused Jacobi passes included) with the ghost
+    planes pushed by the copy engines into the neighbours' mapped buffers and flag-ordered on
+    the GPU: the gathered result equals the single-grid oracle bit for bit, and no bounded wait
+    for a neighbour's flag expired."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res, procs = _spawn(world, "copy")
     assert res == [True] * len(_programs())
     assert all(p.exitcode == 0 for p in procs)
 
