@@ -283,8 +283,8 @@ struct MarchArgs {
   int balanced;
   unsigned* err;
   int vec_store;  // output rows are 16-byte aligned and contiguous in x
-  PeerStore peer;  // slab sweeps with peer stores (the PEER kernel); chunks then run last to first, so
-                  // the boundary chunks sit at both ends of the launch
+  PeerStore peer;  // slab sweeps with peer stores (the PEER kernel); the two boundary chunks then
+                  // run first (chunk 0, the last chunk, then the interior chunks in order)
 };
 
 // Balanced contiguous range of CTA b among G CTAs over W units.
@@ -873,7 +873,10 @@ __global__ void __launch_bounds__(C::THREADS, PEER ? 1 : C::MINB)
       w = seg_end;
     } else {
       tile = w % tiles;
-      const long long c_idx = PEER ? a.work / tiles - 1 - w / tiles : w / tiles;
+      // PEER: boundary chunks first, so their planes reach the neighbours early in the launch
+      // and the neighbours' next launch finds them there without waiting.
+      const long long ci = w / tiles, nch = a.work / tiles;
+      const long long c_idx = !PEER || ci == 0 ? ci : (ci == 1 ? nch - 1 : ci - 1);
       mb = g.m_lo + c_idx * a.chunk;
       me = mb + a.chunk < g.m_hi ? mb + a.chunk : g.m_hi;
       w += gridDim.x;

@@ -329,9 +329,9 @@ int launch_march(const LaunchReq& r) {
   if (r.peer) {
     a.peer = *r.peer;
     if (a.peer.delta_lo % 16 != 0 || a.peer.delta_hi % 16 != 0) a.vec_store = 0;  // remote rows aligned too
-    // Chunks run last to first: the upper-boundary chunk (which reads the upper neighbour's
-    // planes only at its end) leads, the lower-boundary chunk (which reads the lower neighbour's
-    // planes first) closes the launch.  Count the items storing to each side.
+    // The lower and upper boundary chunks run first (their planes reach the neighbours early,
+    // and the neighbours' next launch reads them without waiting).  Count the items storing to
+    // each side.
     const long long nchunks = a.work / tiles;
     long long lo = 0, hi = 0;
     for (long long ci = 0; ci < nchunks; ++ci) {

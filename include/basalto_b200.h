@@ -286,7 +286,8 @@ BST_API int bst_slab_sweeps_deep(bst_comm* c, const bst_program* prog, int32_t d
  * ghost planes first wait (one thread, bounded at about 2 s; a timeout sets the error bit
  * bst_device_error_check reports) until the neighbour's flag shows its previous sweep, which
  * both delivered those planes and finished reading the ghost planes this sweep overwrites.
- * Items run last chunk first, so the waits fall at the two ends of the launch.
+ * The two boundary chunks run first, so their planes reach the neighbours early and the
+ * neighbours' next sweep normally finds its flags already set.
  * Every buffer a sweep writes (b, and a when nsteps >= 2) must be registered with this
  * geometry; a's ghost planes must hold the neighbours' planes of the input (for example after
  * bst_halo_exchange).  Each rank must own at least 2 x ghost planes; ghost >= the axis-0
