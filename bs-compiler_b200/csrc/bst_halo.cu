@@ -103,6 +103,10 @@ struct bst_comm {
   // interior launch of the same pass.
   cudaStream_t bnd_stream = nullptr;
   cudaEvent_t ev_b[2] = {nullptr, nullptr}, ev_int = nullptr;
+  // Copy transport: the upper side's boundary launch and copy get a stream pair of their own
+  // (created on first use), so both sides' rows and copies proceed in parallel.
+  cudaStream_t bnd2_stream = nullptr, comm2_stream = nullptr;
+  cudaEvent_t ev_w = nullptr, ev_b2 = nullptr, ev_comm2 = nullptr;
   // Optional per-pass timing (bst_comm_profile_begin/end): six timing events per pass —
   // boundary start/end, exchange start/end, interior start/end.
   std::vector<cudaEvent_t> prof;
@@ -310,6 +314,21 @@ static void release_cuda(bst_comm* c) {
   if (c->ev_int) cudaEventDestroy(c->ev_int);
   if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
   if (c->bnd_stream) cudaStreamDestroy(c->bnd_stream);
+  for (cudaEvent_t ev : {c->ev_w, c->ev_b2, c->ev_comm2})
+    if (ev) cudaEventDestroy(ev);
+  if (c->bnd2_stream) cudaStreamDestroy(c->bnd2_stream);
+  if (c->comm2_stream) cudaStreamDestroy(c->comm2_stream);
+}
+
+static int ensure_copy_streams(bst_comm* c) {
+  if (c->comm2_stream) return BST_OK;
+  int least = 0, greatest = 0;
+  BST_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  BST_CUDA(cudaStreamCreateWithPriority(&c->bnd2_stream, cudaStreamNonBlocking, greatest));
+  for (cudaEvent_t* ev : {&c->ev_w, &c->ev_b2, &c->ev_comm2})
+    BST_CUDA(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+  BST_CUDA(cudaStreamCreateWithFlags(&c->comm2_stream, cudaStreamNonBlocking));
+  return BST_OK;
 }
 
 extern "C" {
@@ -595,50 +614,76 @@ static int slab_passes(bst_comm* c, const bst_program* prog, int32_t dtype, int3
   BST_CUDA(cudaEventRecord(c->ev_int, st));  // src (with its ghosts) is ready on the caller's stream
   int k = 0;
   int cur = 0;  // index of src in {a, b}
+  if (copy && (rc = ensure_copy_streams(c))) return rc;
   for (int kk : plan) {
     void* out = dst + ghost_bytes;
-    unsigned long long q = 0;
     if (copy) {
-      q = ++c->seq;
+      // Copy-transport pass: lower side on (bnd, comm), upper side on (bnd2, comm2).
+      const unsigned long long q = ++c->seq;
+      const bst_comm::PeerSlab* dr = reg[1 - cur];
+      const size_t pb = size_t(plane) * es;
       if (k > 0) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));  // own copies out of dst
       slab_flags_wait_kernel<<<1, 32, 0, c->bnd_stream>>>(has_lo ? c->flags + 0 : nullptr,
                                                           has_hi ? c->flags + 1 : nullptr, q - 1, err);
       BST_CUDA(cudaGetLastError());
-    }
-    BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
-    if (k > 0 && exchange && !copy) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
-    BST_CUDA(prof_mark(c, 0, c->bnd_stream));
-    rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
-    if (!rc && hi_begin < nl)
-      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd_stream);
-    if (rc) return rc;
-    BST_CUDA(prof_mark(c, 1, c->bnd_stream));
-    BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
-    if (exchange) {
-      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
-      BST_CUDA(prof_mark(c, 2, c->comm_stream));
-      if (copy) {
-        const bst_comm::PeerSlab* dr = reg[1 - cur];
-        const size_t pb = size_t(plane) * es;
-        // owned planes [0, gx) -> rank-1's upper ghost planes; [nl - gx, nl) -> rank+1's lower ones
-        if (has_lo)
-          BST_CUDA(cudaMemcpyAsync(dr->lo + size_t(dr->g_lo + dr->n_lo) * pb, dst + ghost_bytes, size_t(gx) * pb,
-                                   cudaMemcpyDeviceToDevice, c->comm_stream));
-        if (has_hi)
-          BST_CUDA(cudaMemcpyAsync(dr->hi + size_t(dr->g_hi - gx) * pb, dst + ghost_bytes + size_t(nl - gx) * pb,
-                                   size_t(gx) * pb, cudaMemcpyDeviceToDevice, c->comm_stream));
-        slab_flags_set_kernel<<<1, 32, 0, c->comm_stream>>>(has_lo ? c->flag_lo_remote : nullptr,
-                                                            has_hi ? c->flag_hi_remote : nullptr, q);
-        BST_CUDA(cudaGetLastError());
-      } else {
-        rc = halo_enqueue(c, dst, dtype, plane, nl, int32_t(gx), c->comm_stream);
+      BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
+      BST_CUDA(cudaEventRecord(c->ev_w, c->bnd_stream));
+      BST_CUDA(cudaStreamWaitEvent(c->bnd2_stream, c->ev_w, 0));
+      BST_CUDA(prof_mark(c, 0, c->bnd_stream));
+      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
+      if (rc) return rc;
+      BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+      if (hi_begin < nl) {
+        rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd2_stream);
         if (rc) return rc;
       }
+      BST_CUDA(cudaEventRecord(c->ev_b2, c->bnd2_stream));
+      BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_b2, 0));  // boundary end mark covers both sides
+      BST_CUDA(prof_mark(c, 1, c->bnd_stream));
+      // owned planes [nl - gx, nl) -> rank+1's lower ghost planes, then its flag
+      BST_CUDA(cudaStreamWaitEvent(c->comm2_stream, c->ev_b2, 0));
+      if (has_hi) {
+        BST_CUDA(cudaMemcpyAsync(dr->hi + size_t(dr->g_hi - gx) * pb, dst + ghost_bytes + size_t(nl - gx) * pb,
+                                 size_t(gx) * pb, cudaMemcpyDeviceToDevice, c->comm2_stream));
+        slab_flags_set_kernel<<<1, 32, 0, c->comm2_stream>>>(nullptr, c->flag_hi_remote, q);
+        BST_CUDA(cudaGetLastError());
+      }
+      BST_CUDA(cudaEventRecord(c->ev_comm2, c->comm2_stream));
+      // owned planes [0, gx) -> rank-1's upper ghost planes, then its flag
+      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
+      BST_CUDA(prof_mark(c, 2, c->comm_stream));
+      if (has_lo) {
+        BST_CUDA(cudaMemcpyAsync(dr->lo + size_t(dr->g_lo + dr->n_lo) * pb, dst + ghost_bytes, size_t(gx) * pb,
+                                 cudaMemcpyDeviceToDevice, c->comm_stream));
+        slab_flags_set_kernel<<<1, 32, 0, c->comm_stream>>>(c->flag_lo_remote, nullptr, q);
+        BST_CUDA(cudaGetLastError());
+      }
+      BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_comm2, 0));  // ev_comm covers both sides
       BST_CUDA(prof_mark(c, 3, c->comm_stream));
       BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
+      // interior rows after both sides' boundary rows
+      BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[k % 2], 0));
+      BST_CUDA(cudaStreamWaitEvent(st, c->ev_b2, 0));
+    } else {
+      BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_int, 0));
+      if (k > 0 && exchange) BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_comm, 0));
+      BST_CUDA(prof_mark(c, 0, c->bnd_stream));
+      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
+      if (!rc && hi_begin < nl)
+        rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd_stream);
+      if (rc) return rc;
+      BST_CUDA(prof_mark(c, 1, c->bnd_stream));
+      BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+      if (exchange) {
+        BST_CUDA(cudaStreamWaitEvent(c->comm_stream, c->ev_b[k % 2], 0));
+        BST_CUDA(prof_mark(c, 2, c->comm_stream));
+        rc = halo_enqueue(c, dst, dtype, plane, nl, int32_t(gx), c->comm_stream);
+        if (rc) return rc;
+        BST_CUDA(prof_mark(c, 3, c->comm_stream));
+        BST_CUDA(cudaEventRecord(c->ev_comm, c->comm_stream));
+      }
+      if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
     }
-    if (copy) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[k % 2], 0));  // boundary rows first (see above)
-    else if (k > 0) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
     BST_CUDA(prof_mark(c, 4, st));
     if (lo_end < hi_begin) {
       rc = launch_fused(k_canon, dtype, src, s, out, s, kk, lo_end, hi_begin, row_lo, row_hi, st);
@@ -657,6 +702,7 @@ static int slab_passes(bst_comm* c, const bst_program* prog, int32_t dtype, int3
     cur = 1 - cur;
     ++k;
   }
+  if (k > 0 && copy) BST_CUDA(cudaStreamWaitEvent(st, c->ev_b2, 0));
   if (k > 0) {
     BST_CUDA(cudaStreamWaitEvent(st, c->ev_b[(k - 1) % 2], 0));
     if (exchange) BST_CUDA(cudaStreamWaitEvent(st, c->ev_comm, 0));
