@@ -413,7 +413,10 @@ __device__ __forceinline__ EvalCoefs<T, C> eval_coefs(const Coefs<T, C::shape::N
   if constexpr (C::PAIR) {
     Coefs<float2, C::shape::NTERMS> p;
 #pragma unroll
-    for (int g = 0; g < C::shape::NTERMS; ++g) p.scale[g] = make_float2(c.scale[g], c.scale[g]);
+    for (int g = 0; g < C::shape::NTERMS; ++g) {
+      p.scale[g] = make_float2(c.scale[g], c.scale[g]);
+      p.rcp[g] = make_float2(c.rcp[g], c.rcp[g]);
+    }
     p.init_zero = c.init_zero;
     p.negzero = make_float2(c.negzero, c.negzero);
     return p;

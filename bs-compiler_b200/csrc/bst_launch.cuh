@@ -35,7 +35,13 @@ inline int peer_unsupported(const LaunchReq& r, const char* kernel) {
 template <typename T, int N>
 Coefs<T, N> make_coefs(const Canon& c) {
   Coefs<T, N> k{};
-  for (int g = 0; g < c.nterms && g < N; ++g) k.scale[g] = T(c.scale[g]);
+  for (int g = 0; g < c.nterms && g < N; ++g) {
+    k.scale[g] = T(c.scale[g]);
+    // div_by's reciprocal: fp32 divisors with |d| in [2^-60, 2^60] (0 = plain IEEE division)
+    const float d = float(c.scale[g]);
+    const float ad = d < 0.f ? -d : d;
+    if (sizeof(T) == 4 && c.terms[g].op == kDiv && ad >= 0x1p-60f && ad <= 0x1p60f) k.rcp[g] = T(1.0f / d);
+  }
   k.init_zero = c.init_zero;
   k.negzero = T(-0.0);
   return k;

@@ -168,7 +168,7 @@ __device__ __forceinline__ T eval_term(const F& f, const Coefs<T, S::NTERMS>& c)
   T s = term_sum<S, G, T>(f, std::make_integer_sequence<int, cnt - 1>{});
   constexpr int op = S::tbl.terms[G].op;
   if constexpr (op == kMul) return product_rn(c.scale[G], s, c.negzero);
-  else if constexpr (op == kDiv) return div_rn(s, c.scale[G]);
+  else if constexpr (op == kDiv) return div_by(s, c.scale[G], c.rcp[G]);
   else return s;
 }
 

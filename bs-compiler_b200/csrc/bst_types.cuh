@@ -63,6 +63,7 @@ struct Coefs {
   T scale[N];
   int init_zero;
   T negzero;  // -0.0, passed from the host so the compiler cannot fold it (product_rn)
+  T rcp[N];   // fp32 division terms: RN(1 / scale) for div_by, 0 where the divisor is out of its range
 };
 
 // Runtime-table program for the generic kernels (lives in device memory).
@@ -87,6 +88,29 @@ __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, 
 __device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
 __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ double div_rn(double a, double b) { return __ddiv_rn(a, b); }
+// Correctly rounded x / d for an fp32 divisor fixed per launch, from y = RN(1/d) (host IEEE
+// division), by two quotient corrections (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; the correction theorem
+// as proved in Cornea, Golliver and Markstein, ARITH-14, 1999):
+//  * q0 = RN(x y) lies within 1.5 ulp of x/d, and q0 + r0 y, with r0 = RN(x - q0 d), differs
+//    from x/d by (q0 - x/d)(1 - d y) plus r0's rounding, a few 2^-24 ulp, so q1 = RN(q0 + r0 y)
+//    is a faithful (within 1 ulp) quotient;
+//  * for a faithful q1 the remainder r1 = x - q1 d is exact in an fma, and with y within half an
+//    ulp of 1/d the theorem gives RN(q1 + r1 y) = RN(x / d).
+// Nothing under- or overflows while |x| and |d| lie in [2^-60, 2^60]; the host passes y = 0 for
+// other divisors and other x (zeros, subnormals, infinities, NaN) take IEEE division.
+__device__ __forceinline__ float div_by(float x, float d, float y) {
+  const float ax = fabsf(x);
+  if (y != 0.f && ax >= 0x1p-60f && ax <= 0x1p60f) {
+    const float q0 = __fmul_rn(x, y);
+    const float r0 = __fmaf_rn(-q0, d, x);
+    const float q1 = __fmaf_rn(r0, y, q0);
+    const float r1 = __fmaf_rn(-q1, d, x);
+    return __fmaf_rn(r1, y, q1);
+  }
+  return __fdiv_rn(x, d);
+}
+__device__ __forceinline__ double div_by(double x, double d, double) { return __ddiv_rn(x, d); }
 // a * b + c with one rounding (used only for BST_PROGRAM_CONTRACT programs).
 __device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
 __device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
@@ -102,6 +126,9 @@ __device__ __forceinline__ double fma_rn(double a, double b, double c) { return 
 __device__ __forceinline__ float2 add_rn(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 div_rn(float2 a, float2 b) {
   return make_float2(__fdiv_rn(a.x, b.x), __fdiv_rn(a.y, b.y));
+}
+__device__ __forceinline__ float2 div_by(float2 a, float2 b, float2 y) {
+  return make_float2(div_by(a.x, b.x, y.x), div_by(a.y, b.y, y.y));
 }
 __device__ __forceinline__ float2 fma_rn(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
