@@ -494,8 +494,11 @@ def run_basalto(args):
         owners = [partition(gshape[0], ws, r) for r in range(ws)]
         my_start, n_local = owners[rank]
         transport = args.transport
-        if transport == "auto":  # NCCL side-stream exchange: measured ahead of peer stores on every 3-D workload
-            transport = "nccl"
+        if transport == "auto":
+            # Measured on B200: at 2 GPUs the NCCL path (boundary launches concurrent with the
+            # interior) leads; from 4 GPUs on the copy engines match or beat it, since NCCL's
+            # kernel and the boundary launches then wait for SMs the interior launch holds.
+            transport = "nccl" if ws <= 2 else "copy"
         G = slab_ghost_depth(prog, gshape, ws, dt) if transport != "peer" else R[0]
         if args.ghost:
             smallest = min(o[1] for o in owners)
@@ -906,7 +909,8 @@ def main():
                     help="N > 1 ghost planes: nccl = boundary planes first, NCCL exchange on a side stream while "
                          "the interior computes (deep halos where sweeps fuse); copy = the same passes with the "
                          "ghost planes pushed by the copy engines over NVLink; peer = one launch per sweep whose "
-                         "boundary items store into the neighbours over NVLink; auto = nccl")
+                         "boundary items store into the neighbours over NVLink; auto = nccl at 2 GPUs, copy "
+                         "from 3 on")
     ap.add_argument("--ghost", type=int, default=0,
                     help="N > 1, NCCL or copy transport: ghost planes per side (a multiple of the axis-0 radius; default: "
                          "the library's fused depth).  Deeper ghosts let the slab sweeps fuse where a temporally "
