@@ -285,6 +285,11 @@ struct MarchArgs {
   int vec_store;  // output rows are 16-byte aligned and contiguous in x
   PeerStore peer;  // slab sweeps with peer stores (the PEER kernel); the two boundary chunks then
                   // run first (chunk 0, the last chunk, then the interior chunks in order)
+  // Item plan (balanced == 0) in two bands: items [0, work1) cover tile columns [0, tiles1) in
+  // chunks of `chunk` planes, items [work1, work) the other columns in chunks of `chunk2`.
+  long long work1;
+  long long chunk2;
+  long long tiles1;
 };
 
 // Balanced contiguous range of CTA b among G CTAs over W units.
@@ -875,13 +880,22 @@ __global__ void __launch_bounds__(C::THREADS, PEER ? 1 : C::MINB)
       me = g.m_lo + (seg_end - tile * a.nm);
       w = seg_end;
     } else {
-      tile = w % tiles;
-      // PEER: boundary chunks first, so their planes reach the neighbours early in the launch
-      // and the neighbours' next launch finds them there without waiting.
-      const long long ci = w / tiles, nch = a.work / tiles;
+      long long ci, chunk = a.chunk;
+      if (w < a.work1) {
+        tile = w % a.tiles1;
+        ci = w / a.tiles1;
+      } else {  // second band
+        const long long v = w - a.work1, tb = tiles - a.tiles1;
+        tile = a.tiles1 + v % tb;
+        ci = v / tb;
+        chunk = a.chunk2;
+      }
+      // PEER (one band): boundary chunks first, so their planes reach the neighbours early in
+      // the launch and the neighbours' next launch finds them there without waiting.
+      const long long nch = a.work / tiles;
       const long long c_idx = !PEER || ci == 0 ? ci : (ci == 1 ? nch - 1 : ci - 1);
-      mb = g.m_lo + c_idx * a.chunk;
-      me = mb + a.chunk < g.m_hi ? mb + a.chunk : g.m_hi;
+      mb = g.m_lo + c_idx * chunk;
+      me = mb + chunk < g.m_hi ? mb + chunk : g.m_hi;
       w += gridDim.x;
     }
     const int tile_x = int(tile % a.tiles_x);
