@@ -239,9 +239,9 @@ struct LaunchReq;
 template <typename T>
 int dispatch_sweep(const LaunchReq& r);
 int dispatch_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer, int64_t m2_lo, int64_t m2_hi);
 int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer);
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer, int64_t m2_lo, int64_t m2_hi);
 int tb_max_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], bool capability);
 int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], bool capability);
 int dispatch_tb_f32(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], int k,
@@ -250,9 +250,10 @@ int dispatch_tb_f64(const Canon& c, const void* x, const int64_t xs[3], void* y,
                     int64_t m_lo, int64_t m_hi, int64_t row_lo, int64_t row_hi, cudaStream_t st);
 
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
-                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer) {
-  if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st, peer);
-  if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st, peer);
+                 const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer,
+                 int64_t m2_lo, int64_t m2_hi) {
+  if (dtype == BST_F32) return dispatch_f32(c, x, xs, y, ys, m_lo, m_hi, st, peer, m2_lo, m2_hi);
+  if (dtype == BST_F64) return dispatch_f64(c, x, xs, y, ys, m_lo, m_hi, st, peer, m2_lo, m2_hi);
   return fail(BST_ERR_UNSUPPORTED, "dtype must be float32 or float64");
 }
 

@@ -3,9 +3,11 @@
 
 namespace bst {
 int dispatch_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3],
-                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer) {
+                 int64_t m_lo, int64_t m_hi, cudaStream_t st, const PeerStore* peer, int64_t m2_lo, int64_t m2_hi) {
   LaunchReq r{&c, x, {xs[0], xs[1], xs[2]}, y, {ys[0], ys[1], ys[2]}, m_lo, m_hi, st};
   r.peer = peer;
+  r.m2_lo = m2_lo;
+  r.m2_hi = m2_hi;
   return dispatch_sweep<double>(r);
 }
 int tb_max_f64(const Canon& c, const void* x, const int64_t xs[3], void* y, const int64_t ys[3], bool capability) {

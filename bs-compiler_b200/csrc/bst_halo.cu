@@ -630,14 +630,22 @@ static int slab_passes(bst_comm* c, const bst_program* prog, int32_t dtype, int3
       BST_CUDA(cudaEventRecord(c->ev_w, c->bnd_stream));
       BST_CUDA(cudaStreamWaitEvent(c->bnd2_stream, c->ev_w, 0));
       BST_CUDA(prof_mark(c, 0, c->bnd_stream));
-      rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
-      if (rc) return rc;
-      BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
-      if (hi_begin < nl) {
-        rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd2_stream);
+      if (kk == 1 && hi_begin < nl && nl - hi_begin == lo_end) {
+        // single sweep: both boundary ranges in one launch (one ramp, fuller waves)
+        rc = launch_sweep(k_canon, dtype, src, s, out, s, 0, lo_end, c->bnd_stream, nullptr, hi_begin, nl);
         if (rc) return rc;
+        BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+        BST_CUDA(cudaEventRecord(c->ev_b2, c->bnd_stream));
+      } else {
+        rc = launch_fused(k_canon, dtype, src, s, out, s, kk, 0, lo_end, row_lo, row_hi, c->bnd_stream);
+        if (rc) return rc;
+        BST_CUDA(cudaEventRecord(c->ev_b[k % 2], c->bnd_stream));
+        if (hi_begin < nl) {
+          rc = launch_fused(k_canon, dtype, src, s, out, s, kk, hi_begin, nl, row_lo, row_hi, c->bnd2_stream);
+          if (rc) return rc;
+        }
+        BST_CUDA(cudaEventRecord(c->ev_b2, c->bnd2_stream));
       }
-      BST_CUDA(cudaEventRecord(c->ev_b2, c->bnd2_stream));
       BST_CUDA(cudaStreamWaitEvent(c->bnd_stream, c->ev_b2, 0));  // boundary end mark covers both sides
       BST_CUDA(prof_mark(c, 1, c->bnd_stream));
       // owned planes [nl - gx, nl) -> rank+1's lower ghost planes, then its flag

@@ -49,9 +49,11 @@ void logical_strides(int ndim, const int64_t* strides, int64_t out[3]);
 
 // Launch one sweep.  x/y strides are logical [M,Y,X]; m range is in output planes.  `peer`:
 // also store every output into a neighbouring GPU's memory (TMA march kernels only).
+// [m2_lo, m2_hi): a second range of output planes (the upper slab boundary rows), in the same
+// launch where the kernel allows (TMA march, ranges of equal length), else a second launch.
 int launch_sweep(const Canon& c, int dtype, const void* x, const int64_t xs[3], void* y,
                  const int64_t ys[3], int64_t m_lo, int64_t m_hi, cudaStream_t st,
-                 const PeerStore* peer = nullptr);
+                 const PeerStore* peer = nullptr, int64_t m2_lo = 0, int64_t m2_hi = 0);
 
 // Temporal blocking.  tb_max_sweeps: most sweeps one launch can fuse for this request
 // (1 = no fused kernel).  launch_fused: k sweeps of output planes [m_lo, m_hi) in one launch

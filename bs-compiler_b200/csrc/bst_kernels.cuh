@@ -290,6 +290,10 @@ struct MarchArgs {
   long long work1;
   long long chunk2;
   long long tiles1;
+  // Two plane ranges in one launch (item schedule): items whose first plane is at or above
+  // gap_at are moved up by gap planes (LLONG_MAX: one range).
+  long long gap_at;
+  long long gap;
 };
 
 // Balanced contiguous range of CTA b among G CTAs over W units.
@@ -896,6 +900,10 @@ __global__ void __launch_bounds__(C::THREADS, PEER ? 1 : C::MINB)
       const long long c_idx = !PEER || ci == 0 ? ci : (ci == 1 ? nch - 1 : ci - 1);
       mb = g.m_lo + c_idx * chunk;
       me = mb + chunk < g.m_hi ? mb + chunk : g.m_hi;
+      if (mb >= a.gap_at) {
+        mb += a.gap;
+        me += a.gap;
+      }
       w += gridDim.x;
     }
     const int tile_x = int(tile % a.tiles_x);

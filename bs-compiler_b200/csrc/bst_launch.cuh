@@ -4,6 +4,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -26,7 +27,24 @@ struct LaunchReq {
   int64_t row_lo = 0, row_hi = -1;
   // Slab boundary launches: also store into a neighbouring GPU's ghost planes (TMA march only).
   const PeerStore* peer = nullptr;
+  // A second range of output planes [m2_lo, m2_hi) in the same request (slab boundary rows):
+  // one launch on the TMA march kernel, two launches elsewhere.
+  int64_t m2_lo = 0, m2_hi = 0;
 };
+
+inline bool two_ranges(const LaunchReq& r) { return r.m2_hi > r.m2_lo; }
+
+// Runs a two-range request as two launches of `launch`.
+template <class F>
+int each_range(const LaunchReq& r, F&& launch) {
+  LaunchReq a = r;
+  a.m2_lo = a.m2_hi = 0;
+  if (int rc = launch(a)) return rc;
+  LaunchReq b = a;
+  b.m_lo = r.m2_lo;
+  b.m_hi = r.m2_hi;
+  return launch(b);
+}
 
 inline int peer_unsupported(const LaunchReq& r, const char* kernel) {
   if (!r.peer) return BST_OK;
@@ -69,6 +87,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 // ---- direct ---------------------------------------------------------------------
 template <typename T, class S>
 int launch_direct(const LaunchReq& r) {
+  if (two_ranges(r)) return each_range(r, [](const LaunchReq& q) { return launch_direct<T, S>(q); });
   if (int rc = peer_unsupported(r, "the direct kernel")) return rc;
   const GridDesc g = make_grid(r);
   const long long total = (r.m_hi - r.m_lo) * g.no[1] * g.no[2];
@@ -85,6 +104,7 @@ int launch_direct(const LaunchReq& r) {
 
 template <typename T>
 int launch_direct_table(const LaunchReq& r) {
+  if (two_ranges(r)) return each_range(r, [](const LaunchReq& q) { return launch_direct_table<T>(q); });
   if (int rc = peer_unsupported(r, "the runtime-table kernel")) return rc;
   const Canon& c = *r.c;
   const GridDesc g = make_grid(r);
@@ -147,6 +167,7 @@ int occupancy(const void* fn, int threads, int smem);  // resident CTAs per SM (
 
 template <typename T, class S, int ORG>
 int launch_line(const LaunchReq& r) {
+  if (two_ranges(r)) return each_range(r, [](const LaunchReq& q) { return launch_line<T, S, ORG>(q); });
   if (int rc = peer_unsupported(r, "the 1-D line kernel")) return rc;
   constexpr int V = Vec16<T>::N;
   LineArgs a{r.c->n[2], r.c->no[2]};
@@ -366,9 +387,13 @@ inline ItemPlan choose_item_plan(long long tiles, long long nm, int rb, int over
 
 template <typename T, class C>
 int launch_march(const LaunchReq& r) {
+  // Two ranges in one launch: equal lengths, the second above the first, no peer stores.
+  const bool pair = two_ranges(r);
+  if (pair && (r.peer || r.m_hi - r.m_lo != r.m2_hi - r.m2_lo || r.m2_lo < r.m_hi))
+    return each_range(r, [](const LaunchReq& q) { return launch_march<T, C>(q); });
   const Canon& c = *r.c;
   constexpr int E = sizeof(T);
-  const long long nm = r.m_hi - r.m_lo;
+  const long long nm = (r.m_hi - r.m_lo) * (pair ? 2 : 1);  // a pair: both ranges, stacked
   if (nm <= 0) return BST_OK;
   CUtensorMap map;
   const cuuint64_t dims[3] = {cuuint64_t(c.n[2]), cuuint64_t(c.n[1]), cuuint64_t(c.n[0])};
@@ -388,6 +413,13 @@ int launch_march(const LaunchReq& r) {
 
   MarchArgs a{};
   a.g = make_grid(r);
+  a.gap_at = LLONG_MAX;
+  if (pair) {  // planes [m_lo, m_lo + 2L) of the launch: the upper half is [m2_lo, m2_hi)
+    const long long len = r.m_hi - r.m_lo;
+    a.g.m_hi = r.m_lo + 2 * len;
+    a.gap_at = r.m_lo + len;
+    a.gap = r.m2_lo - (r.m_lo + len);
+  }
   a.tiles_x = int((c.no[2] + C::TX - 1) / C::TX);
   a.tiles_y = int((c.no[1] + C::TY - 1) / C::TY);
   const int occ = occupancy(reinterpret_cast<const void*>(kern), C::THREADS, C::SMEM);
@@ -396,8 +428,9 @@ int launch_march(const LaunchReq& r) {
   const long long tiles = (long long)a.tiles_x * a.tiles_y;
   a.nm = nm;
   long long grid = 0;
-  // Peer-store sweeps count their boundary items, so they use the item schedule.
-  switch (r.peer ? Schedule::kItems : march_schedule()) {
+  // Peer-store sweeps count their boundary items, so they use the item schedule; a pair of
+  // ranges is one chunk per range and tile column.
+  switch (r.peer || pair ? Schedule::kItems : march_schedule()) {
     case Schedule::kBalanced:
       a.balanced = 1;
       a.work = tiles * nm;
@@ -415,7 +448,10 @@ int launch_march(const LaunchReq& r) {
       [[fallthrough]];
     default: {
       const int overhead = 2 * C::RM + 2 * C::RB + 8;
-      if (r.peer) {  // one band: the peer logic counts items per chunk row
+      if (pair) {
+        a.chunk = r.m_hi - r.m_lo;
+        a.work = tiles * 2;
+      } else if (r.peer) {  // one band: the peer logic counts items per chunk row
         int chunk = 0;
         long long nchunks = 1;
         choose_chunks(tiles, nm, C::RB, overhead, resident, &chunk, &nchunks);
