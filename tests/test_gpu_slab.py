@@ -23,15 +23,20 @@ pytestmark = pytest.mark.gpu
 def _programs():
     from basalto import program as P
     from basalto import workloads as W
+    from basalto.program import StencilProgram, Term
+    # outside the compiled catalog (runtime-table kernel; its boundary ranges run as two launches)
+    odd = StencilProgram(3, (Term("mul", 0.3, ((0, 0, 0), (1, 1, 0))), Term("div", 7.0, ((-1, 0, 2),)),
+                             Term("sum", 0.0, ((0, -2, -1), (2, 0, 0)))))
     return [(P.heat7_3d(), (37, 20, 64), torch.float32, 4),
             (P.jacobi5_2d(), (70, 256), torch.float32, 5),
             (P.box(3, 1, W.box27_weights()), (19, 16, 64), torch.float64, 3),
             (P.star_3d(P.LAPLACIAN8_COEFFS), (21, 24, 128), torch.float32, 2),
             (P.jacobi5_2d(), (64, 128), torch.float64, 7),
-            (P.jacobi5_2d(), (96, 516), torch.float32, 13)]
+            (P.jacobi5_2d(), (96, 516), torch.float32, 13),
+            (odd, (15, 18, 40), torch.float32, 3)]
 
 
-@pytest.mark.parametrize("idx", range(6))
+@pytest.mark.parametrize("idx", range(7))
 def test_single_rank_slab_equals_single_grid(idx):
     from basalto.slab import SlabDomain
     import basalto
