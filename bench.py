@@ -904,7 +904,10 @@ def main():
     ap.add_argument("--shape", default="", help="override the workload's grid, e.g. 512x512x512")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="host work timed for the cpu_baseline field (whole sweeps, at least this long)")
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=10,
+                    help="end-to-end steps timed through the public API with host buffers (pipelined, three "
+                         "buffer sets in flight); the first upload and last download are not overlapped, so "
+                         "more steps approach the streaming rate")
     ap.add_argument("--transport", choices=["auto", "nccl", "copy", "peer"], default="auto",
                     help="N > 1 ghost planes: nccl = boundary planes first, NCCL exchange on a side stream while "
                          "the interior computes (deep halos where sweeps fuse); copy = the same passes with the "
