@@ -108,6 +108,7 @@ SIGNATURES = [
      [c_void_p, POINTER(CProgram), c_int32, c_int32, POINTER(c_int64), c_int32, c_void_p, c_void_p, c_int32,
       c_void_p]),
     ("bst_comm_profile_begin", c_int32, [c_void_p, c_int32]),
+    ("bst_march_item_plan", c_int32, [c_int64, c_int64, c_int32, c_int32, c_int64, POINTER(c_int64)]),
     ("bst_comm_profile_end", c_int32, [c_void_p, POINTER(c_double)]),
 ]
 

@@ -11,6 +11,7 @@
 #include <unordered_map>
 
 #include "bst_internal.h"
+#include "bst_plan.h"
 
 namespace bst {
 
@@ -463,6 +464,21 @@ int bst_stencil_sweeps_fused(const bst_program* prog, int32_t dtype, int32_t ndi
     if (rc) return rc;
     std::swap(src, dst);
   }
+  return BST_OK;
+}
+
+int bst_march_item_plan(int64_t tiles, int64_t planes, int32_t rb, int32_t overhead, int64_t resident,
+                        int64_t out[5]) {
+  clear_error();
+  if (!out) return fail(BST_ERR_INVALID, "null output");
+  if (tiles < 1 || planes < 1 || rb < 1 || overhead < 0 || resident < 1)
+    return fail(BST_ERR_INVALID, "tiles, planes, rb and resident must be positive, overhead non-negative");
+  const ItemPlan p = choose_item_plan(tiles, planes, rb, overhead, resident);
+  out[0] = p.tiles1;
+  out[1] = p.chunk1;
+  out[2] = p.n1;
+  out[3] = p.chunk2;
+  out[4] = p.n2;
   return BST_OK;
 }
 

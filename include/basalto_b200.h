@@ -324,6 +324,15 @@ BST_API int bst_slab_sweeps_copy(bst_comm* c, const bst_program* prog, int32_t d
 BST_API int bst_comm_profile_begin(bst_comm* c, int32_t max_passes);
 BST_API int bst_comm_profile_end(bst_comm* c, double out[6]);
 
+/* The march kernel's work plan for a launch of `tiles` tile columns of `planes` output planes
+ * on `resident` persistent CTAs (diagnostics; host only): out[0] tile columns in the first
+ * band, out[1] its chunk length in planes, out[2] its chunks per column, out[3] and out[4] the
+ * same for the other columns.  Chunks are whole multiples of rb planes (the last one of a
+ * column may be shorter); overhead is the per-item ramp, in planes, of the launch model that
+ * picks the plan.  One band when out[0] == tiles. */
+BST_API int bst_march_item_plan(int64_t tiles, int64_t planes, int32_t rb, int32_t overhead, int64_t resident,
+                                int64_t out[5]);
+
 #ifdef __cplusplus
 }
 #endif
