@@ -16,7 +16,7 @@
 //    overlap on the GPU race (use one stream, or order the calls).  Each call rewrites the
 //    whole header and every entry the kernel reads, so nothing left by an earlier call is used;
 //  * the first call on a device looks up the array's device address (cudaGetSymbolAddress)
-//    with that device current.
+//    with that device current; that first call should come before any stream capture begins.
 // Every GPU that loads the library holds the 32 KiB array until the process exits.
 #include <cuda_runtime.h>
 

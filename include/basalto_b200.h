@@ -136,7 +136,8 @@ BST_API int bst_stencil_apply(const bst_program* prog, int32_t dtype, int32_t nd
  * + 5*nterms + elem*nterms bytes, aligned) exceeds 32 KiB return BST_ERR_UNSUPPORTED.
  * The array is shared by every call on the device: calls whose work overlaps on the GPU
  * (different streams, unordered) race; each call rewrites all the table it uses.  The first
- * call on a device looks up the array's device address. */
+ * call on a device looks up the array's device address (set-up); make that first call before
+ * any stream capture begins. */
 BST_API int bst_stencil_apply_noalloc(const bst_program* prog, int32_t dtype, int32_t ndim,
                                       const int64_t* shape, const int64_t* x_strides, const void* x,
                                       const int64_t* y_strides, void* y, void* stream);
