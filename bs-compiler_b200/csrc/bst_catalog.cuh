@@ -140,10 +140,15 @@ using CfgBox = Cfg3D<T, S, BST_BOX_TY, BST_BOX_PY, BST_BOX_NSX, bool(BST_BOX_HAL
 #ifndef BST_STAR_INTERLEAVE
 #define BST_STAR_INTERLEAVE 0  // 1: a plane's point pairs fold term by term together; 2: all planes of a group do
 #endif
+#ifndef BST_STAR_VXB
+#define BST_STAR_VXB 16  // fp32 lane vector bytes: 8 = two x points per lane (half the window registers)
+#endif
+template <typename T>
+constexpr int kStarVXB = sizeof(T) == 4 ? BST_STAR_VXB : 16;
 template <typename T, class S>
-using CfgStar = MarchCfg<T, S, kRowCols<T>, BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX, bool(BST_STAR_HALO_LDS),
-                         false, bool(BST_STAR_WINDOW), BST_STAR_MINB, bool(BST_STAR_PAIR), bool(BST_STAR_CIRC),
-                         BST_STAR_INTERLEAVE>;
+using CfgStar = MarchCfg<T, S, 32 * kStarVXB<T> / int(sizeof(T)), BST_STAR_TY, BST_STAR_PY, BST_STAR_RB, BST_STAR_NSX,
+                         bool(BST_STAR_HALO_LDS), false, bool(BST_STAR_WINDOW), BST_STAR_MINB, bool(BST_STAR_PAIR),
+                         bool(BST_STAR_CIRC), BST_STAR_INTERLEAVE, kStarVXB<T>>;
 // Boxes in ascending order stream: each input plane is applied to every output it touches as
 // it arrives (stream_mode in bst_kernels.cuh); descending boxes keep the per-output gather.
 #ifndef BST_BOXS_TY

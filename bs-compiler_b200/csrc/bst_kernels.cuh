@@ -192,15 +192,16 @@ constexpr auto pick_segs() {
 // HALO_LDS: a row's x-halo comes as whole neighbouring vectors from shared memory (one
 // ld.shared.v4 each) instead of shuffles plus edge-lane loads; cheaper in issue slots for
 // wide radii, dearer in shared-memory bandwidth.
+// VXB_: bytes of one lane's vector of consecutive x points (16; 8 halves a lane's registers).
 template <typename T, class S, int TX_, int TY_, int PY_, int RB_, int NSX_, bool HALO_LDS_ = false,
           bool STREAM_ = false, bool WINDOW_ = true, int MINB_ = 1, bool PAIR_ = false, bool CIRC_ = false,
-          int INTERLEAVE_ = 0>
+          int INTERLEAVE_ = 0, int VXB_ = 16>
 struct MarchCfg {
   using shape = S;
   static constexpr int MINB = MINB_;  // CTAs per SM the register allocation must allow
   static constexpr bool HALO_LDS = HALO_LDS_;
   static constexpr bool STREAM = STREAM_ && stream_mode<S>();
-  static constexpr int VX = 16 / int(sizeof(T));   // elements per 16-byte vector
+  static constexpr int VX = VXB_ / int(sizeof(T));  // elements per lane vector
   static constexpr int TX = TX_;                   // output columns per tile
   static constexpr int TY = TY_;                   // output rows per tile
   static constexpr int PY = PY_;                   // rows per thread
@@ -316,6 +317,26 @@ struct Vec16<double> {
   static constexpr int N = 2;
 };
 
+// N consecutive elements of T moved by one 8- or 16-byte access.
+template <typename T, int N>
+struct VecN;
+template <>
+struct VecN<float, 4> {
+  using type = float4;
+};
+template <>
+struct VecN<float, 2> {
+  using type = float2;
+};
+template <>
+struct VecN<double, 2> {
+  using type = double2;
+};
+template <>
+struct VecN<double, 1> {
+  using type = double;
+};
+
 // Per-thread register state of the march: window and row segments.
 template <typename T, class C>
 struct MarchRegs {
@@ -346,7 +367,7 @@ struct PointFetch {
 
 template <typename T, int N>
 __device__ __forceinline__ void lds_vec(const T* p, T (&v)[N]) {
-  using VT = typename Vec16<T>::type;
+  using VT = typename VecN<T, N>::type;
   const VT q = *reinterpret_cast<const VT*>(p);
   const T* e = reinterpret_cast<const T*>(&q);
 #pragma unroll
@@ -459,7 +480,7 @@ __device__ __forceinline__ void eval_row(const MarchRegs<T, C>& r, const EvalCoe
 template <typename T, class C>
 __device__ __forceinline__ void store_row(T* d, const T (&res)[C::VX], bool interior, bool row_ok, int cols_left,
                                           long long so2, long long pd) {
-  using VT = typename Vec16<T>::type;
+  using VT = typename VecN<T, C::VX>::type;
   if (interior) {
     VT q;
     T* e = reinterpret_cast<T*>(&q);
@@ -684,7 +705,7 @@ __device__ __forceinline__ void peer_copy(T* out, const GridDesc& g, int x0, int
   const int cols = (int)(g.no[2] - x0 < C::TX ? g.no[2] - x0 : C::TX);
   if (m1 <= m0 || rows <= 0 || cols <= 0) return;
   if (vec && cols == C::TX) {
-    using VT = typename Vec16<T>::type;
+    using VT = typename VecN<T, C::VX>::type;
     constexpr int NV = C::TX / C::VX;
     const long long total = (m1 - m0) * rows * NV;
     for (long long i = threadIdx.x; i < total; i += C::THREADS) {
